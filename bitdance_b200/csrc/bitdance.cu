@@ -1,0 +1,358 @@
+// bitdance.cu -- the C ABI of the library (include/bitdance_b200.h): argument checks,
+// tensor-map set-up and launches of the kernels in transcode.cuh and gemm.cuh.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/bitdance_b200.h"
+#include "gemm.cuh"
+#include "sm100.cuh"
+#include "transcode.cuh"
+
+namespace bd {
+
+// Error word that kernels OR their error bits into (one per device that loads the library).
+__device__ uint32_t g_err_word;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+inline cudaStream_t as_stream(bd_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned(const void* p, uintptr_t a) {
+  return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
+}
+
+// Per-device facts, computed once.
+struct DeviceInfo {
+  int sm_count = 0;
+  bool is_sm100 = false;
+  uint32_t* err = nullptr;
+  bool ready = false;
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_info(DeviceInfo** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BD_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ready) {
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return BD_ERR_CUDA;
+    d.is_sm100 = (major == 10 && minor == 0);
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_err_word) != cudaSuccess) return BD_ERR_CUDA;
+    d.err = static_cast<uint32_t*>(p);
+    d.ready = true;
+  }
+  *out = &d;
+  return d.is_sm100 ? BD_OK : BD_ERR_ARCH;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda needed).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+bool make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, void* base, uint64_t d0, uint64_t d1,
+                 uint64_t stride1_bytes, uint32_t b0, uint32_t b1, CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {d0, d1};
+  const cuuint64_t strides[1] = {stride1_bytes};
+  const cuuint32_t box[2] = {b0, b1};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int grid_for(int64_t work, int per_block, const DeviceInfo* d) {
+  int64_t blocks = (work + per_block - 1) / per_block;
+  const int64_t cap = static_cast<int64_t>(d->sm_count) * 8;
+  if (blocks > cap) blocks = cap;
+  return static_cast<int>(blocks < 1 ? 1 : blocks);
+}
+
+int token_tile(int M) {
+  if (M <= 16) return 16;
+  if (M <= 32) return 32;
+  if (M <= 64) return 64;
+  if (M <= 128) return 128;
+  return 256;
+}
+
+int choose_split(int M, int N, int K, int sm_count) {
+  const int nkt = K / 128;
+  const int bn = token_tile(M);
+  const int64_t tiles = static_cast<int64_t>(N / 128) * ((M + bn - 1) / bn);
+  if (tiles >= sm_count) return 1;
+  int best = 1;
+  double best_score = 0.0;
+  for (int s = 1; s <= nkt; ++s) {
+    if (nkt % s) continue;
+    if (s > 1 && nkt / s < 4) break;
+    const int64_t ctas = tiles * s;
+    const int64_t waves = (ctas + sm_count - 1) / sm_count;
+    double score = static_cast<double>(ctas) / static_cast<double>(waves * sm_count);
+    score -= 0.02 * (s > 1 ? 1 : 0);  // the reduction pass is not free
+    if (score > best_score + 1e-9) {
+      best_score = score;
+      best = s;
+    }
+  }
+  return best;
+}
+
+template <int BN>
+int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tas, const GemmParams& p, int M,
+                   int N, int split, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    if (cudaFuncSetAttribute(w4a6_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg::kSmemBytes) != cudaSuccess)
+      return BD_ERR_CUDA;
+    configured.fetch_or(bit);
+  }
+  const dim3 grid(N / 128, (M + BN - 1) / BN, split);
+  w4a6_gemm_kernel<BN><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tas, p);
+  return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
+}
+
+}  // namespace
+}  // namespace bd
+
+using namespace bd;
+
+extern "C" {
+
+int bd_version(void) { return 100; }
+
+const char* bd_status_string(int status) {
+  switch (status) {
+    case BD_OK: return "ok";
+    case BD_ERR_INVALID_ARG: return "invalid argument";
+    case BD_ERR_SHAPE: return "unsupported shape";
+    case BD_ERR_ALIGNMENT: return "misaligned pointer";
+    case BD_ERR_ARCH: return "device is not sm_100 (B200)";
+    case BD_ERR_CUDA: return "CUDA runtime error";
+    case BD_ERR_WORKSPACE: return "workspace missing or too small";
+    case BD_ERR_DEVICE: return "a kernel reported an error";
+    default: return "unknown status";
+  }
+}
+
+int bd_device_error(uint32_t* word, int clear) {
+  if (word == nullptr) return BD_ERR_INVALID_ARG;
+  DeviceInfo* d = nullptr;
+  int st = device_info(&d);
+  if (st != BD_OK) return st;
+  if (cudaDeviceSynchronize() != cudaSuccess) return BD_ERR_CUDA;
+  if (cudaMemcpy(word, d->err, sizeof(uint32_t), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return BD_ERR_CUDA;
+  if (clear && cudaMemset(d->err, 0, sizeof(uint32_t)) != cudaSuccess) return BD_ERR_CUDA;
+  return BD_OK;
+}
+
+int bd_transcode_nvfp4_to_mxfp6(const uint8_t* codes, const uint8_t* scales, uint8_t* e2m3_out,
+                                uint8_t* e8m0_out, int64_t nblk32, int scale_block,
+                                bd_stream_t stream) {
+  if (scale_block != 16 && scale_block != 32) return BD_ERR_INVALID_ARG;
+  if (nblk32 < 0) return BD_ERR_SHAPE;
+  if (nblk32 == 0) return BD_OK;
+  if (!codes || !scales || !e2m3_out || !e8m0_out) return BD_ERR_INVALID_ARG;
+  if (!aligned(codes, 16) || !aligned(e2m3_out, 16) || (scale_block == 16 && !aligned(scales, 2)))
+    return BD_ERR_ALIGNMENT;
+  DeviceInfo* d = nullptr;
+  int st = device_info(&d);
+  if (st != BD_OK) return st;
+  const int grid = grid_for(nblk32, 256, d);
+  if (scale_block == 16)
+    transcode_kernel<16><<<grid, 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const uint4*>(codes), scales, reinterpret_cast<uint4*>(e2m3_out),
+        e8m0_out, nblk32);
+  else
+    transcode_kernel<32><<<grid, 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const uint4*>(codes), scales, reinterpret_cast<uint4*>(e2m3_out),
+        e8m0_out, nblk32);
+  return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
+}
+
+int bd_pack_b(const uint8_t* codes, const uint8_t* scales16, uint8_t* codes_tiled,
+              uint8_t* scales_tiled, int N, int K, bd_stream_t stream) {
+  if (!codes || !scales16 || !codes_tiled || !scales_tiled) return BD_ERR_INVALID_ARG;
+  if (N <= 0 || K <= 0 || N % 128 || K % 128) return BD_ERR_SHAPE;
+  if (!aligned(codes, 16) || !aligned(codes_tiled, 16) || !aligned(scales16, 8) ||
+      !aligned(scales_tiled, 8))
+    return BD_ERR_ALIGNMENT;
+  DeviceInfo* d = nullptr;
+  int st = device_info(&d);
+  if (st != BD_OK) return st;
+  const int64_t work = static_cast<int64_t>(N) * (K / 128);
+  pack_b_kernel<<<grid_for(work, 256, d), 256, 0, as_stream(stream)>>>(codes, scales16,
+                                                                        codes_tiled, scales_tiled,
+                                                                        N, K);
+  return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
+}
+
+int bd_pack_a(const uint8_t* codes, const uint8_t* e8m0, uint8_t* a_packed, uint8_t* scales_tiled,
+              int M, int K, bd_stream_t stream) {
+  if (!codes || !e8m0 || !a_packed || !scales_tiled) return BD_ERR_INVALID_ARG;
+  if (M <= 0 || K <= 0 || K % 128) return BD_ERR_SHAPE;
+  if (!aligned(codes, 16) || !aligned(a_packed, 16) || !aligned(scales_tiled, 4))
+    return BD_ERR_ALIGNMENT;
+  DeviceInfo* d = nullptr;
+  int st = device_info(&d);
+  if (st != BD_OK) return st;
+  const int64_t nchunks = static_cast<int64_t>(M) * K / 16;
+  pack_a_codes_kernel<<<grid_for(nchunks, 256, d), 256, 0, as_stream(stream)>>>(codes, a_packed,
+                                                                                 nchunks);
+  const int Mp4 = (M + 3) / 4 * 4;
+  const int64_t words = static_cast<int64_t>(K / 128) * Mp4;
+  pack_a_scales_kernel<<<grid_for(words, 256, d), 256, 0, as_stream(stream)>>>(e8m0, scales_tiled,
+                                                                                M, Mp4, K);
+  return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
+}
+
+int bd_choose_split_k(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % 128) return BD_ERR_SHAPE;
+  DeviceInfo* d = nullptr;
+  int st = device_info(&d);
+  const int sms = (st == BD_OK || st == BD_ERR_ARCH) && d ? d->sm_count : 148;
+  return choose_split(M, N, K, sms > 0 ? sms : 148);
+}
+
+size_t bd_query_workspace(int M, int N, int K, int split_k, int split_mode) {
+  if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % 128) return 0;
+  if (split_k == 0) split_k = bd_choose_split_k(M, N, K);
+  if (split_k <= 1 || split_mode != BD_SPLIT_REDUCE) return 0;
+  return static_cast<size_t>(split_k) * static_cast<size_t>(M) * static_cast<size_t>(N) *
+         sizeof(float);
+}
+
+int bd_splitk_reduce(const float* partials, void* c, const void* bias, float b_tensor_scale,
+                     int M, int N, int split_k, int out_dtype, int epilogue, bd_stream_t stream) {
+  if (!partials || !c) return BD_ERR_INVALID_ARG;
+  if (out_dtype < BD_OUT_BF16 || out_dtype > BD_OUT_F32) return BD_ERR_INVALID_ARG;
+  if (epilogue < BD_EPI_NONE || epilogue > BD_EPI_BIAS_GELU) return BD_ERR_INVALID_ARG;
+  if (epilogue != BD_EPI_NONE && !bias) return BD_ERR_INVALID_ARG;
+  if (M <= 0 || N <= 0 || N % 4 || split_k < 1) return BD_ERR_SHAPE;
+  if (!aligned(partials, 16)) return BD_ERR_ALIGNMENT;
+  DeviceInfo* d = nullptr;
+  int st = device_info(&d);
+  if (st != BD_OK) return st;
+  const int64_t work = static_cast<int64_t>(M) * N / 4;
+  splitk_reduce_kernel<<<grid_for(work, 256, d), 256, 0, as_stream(stream)>>>(
+      partials, c, static_cast<const __nv_bfloat16*>(bias), b_tensor_scale, M, N, split_k,
+      out_dtype, epilogue);
+  return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
+}
+
+int bd_w4a6_gemm(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8_t* b,
+                 const uint8_t* b_scales, float b_tensor_scale, const void* bias, int M, int N,
+                 int K, int split_k, int split_mode, int out_dtype, int epilogue, void* workspace,
+                 size_t workspace_bytes, bd_stream_t stream) {
+  if (!c || !a || !a_scales || !b || !b_scales) return BD_ERR_INVALID_ARG;
+  if (out_dtype < BD_OUT_BF16 || out_dtype > BD_OUT_F32) return BD_ERR_INVALID_ARG;
+  if (epilogue < BD_EPI_NONE || epilogue > BD_EPI_BIAS_GELU) return BD_ERR_INVALID_ARG;
+  if (epilogue != BD_EPI_NONE && !bias) return BD_ERR_INVALID_ARG;
+  if (split_mode < BD_SPLIT_REDUCE || split_mode > BD_SPLIT_ATOMIC) return BD_ERR_INVALID_ARG;
+  if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % 128) return BD_ERR_SHAPE;
+  if (M > (1 << 30) / 4 || K > (1 << 24) || N > (1 << 24)) return BD_ERR_SHAPE;
+  if (!aligned(a, 16) || !aligned(a_scales, 16) || !aligned(b, 16) || !aligned(b_scales, 16) ||
+      (bias && !aligned(bias, 2)))
+    return BD_ERR_ALIGNMENT;
+  DeviceInfo* d = nullptr;
+  int st = device_info(&d);
+  if (st != BD_OK) return st;
+  const int nkt = K / 128;
+  if (split_k == 0) split_k = choose_split(M, N, K, d->sm_count);
+  if (split_k < 1 || nkt % split_k) return BD_ERR_SHAPE;
+  if (split_mode == BD_SPLIT_ATOMIC && (out_dtype != BD_OUT_F32 || epilogue != BD_EPI_NONE))
+    return BD_ERR_INVALID_ARG;
+  if (split_k > 1 && split_mode == BD_SPLIT_PLANES && epilogue != BD_EPI_NONE)
+    return BD_ERR_INVALID_ARG;
+  const bool use_ws = split_k > 1 && split_mode == BD_SPLIT_REDUCE;
+  if (use_ws) {
+    const size_t need = static_cast<size_t>(split_k) * M * static_cast<size_t>(N) * sizeof(float);
+    if (!workspace || workspace_bytes < need) return BD_ERR_WORKSPACE;
+    if (!aligned(workspace, 16) || N % 4) return BD_ERR_ALIGNMENT;
+  }
+
+  const int bn = token_tile(M);
+  const int Mp4 = (M + 3) / 4 * 4;
+  CUtensorMap ta, tas;
+  if (!make_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, const_cast<uint8_t*>(a), K, M, K, 128, bn,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+    return BD_ERR_CUDA;
+  if (!make_map_2d(&tas, CU_TENSOR_MAP_DATA_TYPE_UINT32, const_cast<uint8_t*>(a_scales), Mp4,
+                   nkt, static_cast<uint64_t>(Mp4) * 4, bn, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return BD_ERR_CUDA;
+
+  GemmParams p;
+  p.wcodes = b;
+  p.wscales = b_scales;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.tensor_scale = b_tensor_scale;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ktiles = nkt / split_k;
+  p.out_dtype = out_dtype;
+  p.epilogue = epilogue;
+  p.err = d->err;
+  if (split_mode == BD_SPLIT_ATOMIC) {
+    p.out_mode = kOutAtomic;  // accumulates into c even at split_k == 1
+    p.out = c;
+  } else if (split_k == 1) {
+    p.out_mode = kOutC;
+    p.out = c;
+  } else if (split_mode == BD_SPLIT_REDUCE) {
+    p.out_mode = kOutPartial;
+    p.out = workspace;
+  } else {
+    p.out_mode = kOutPlane;
+    p.out = c;
+  }
+  cudaStream_t s = as_stream(stream);
+  int rc;
+  switch (bn) {
+    case 16: rc = launch_gemm_bn<16>(ta, tas, p, M, N, split_k, s); break;
+    case 32: rc = launch_gemm_bn<32>(ta, tas, p, M, N, split_k, s); break;
+    case 64: rc = launch_gemm_bn<64>(ta, tas, p, M, N, split_k, s); break;
+    case 128: rc = launch_gemm_bn<128>(ta, tas, p, M, N, split_k, s); break;
+    default: rc = launch_gemm_bn<256>(ta, tas, p, M, N, split_k, s); break;
+  }
+  if (rc != BD_OK || !use_ws) return rc;
+  return bd_splitk_reduce(static_cast<const float*>(workspace), c, bias, b_tensor_scale, M, N,
+                          split_k, out_dtype, epilogue, stream);
+}
+
+}  // extern "C"

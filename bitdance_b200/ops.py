@@ -1,0 +1,160 @@
+"""Tensor-level entry points over the C ABI (device buffers are torch CUDA tensors).
+
+PyTorch only provides device memory and the current stream here; every computation runs
+in the library's own CUDA kernels.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import call
+
+_OUT = {torch.bfloat16: _lib.BD_OUT_BF16, torch.float16: _lib.BD_OUT_F16,
+        torch.float32: _lib.BD_OUT_F32}
+EPILOGUES = {"none": _lib.BD_EPI_NONE, "bias": _lib.BD_EPI_BIAS,
+             "bias_relu": _lib.BD_EPI_BIAS_RELU, "bias_silu": _lib.BD_EPI_BIAS_SILU,
+             "bias_gelu": _lib.BD_EPI_BIAS_GELU}
+SPLIT_MODES = {"reduce": _lib.BD_SPLIT_REDUCE, "planes": _lib.BD_SPLIT_PLANES,
+               "atomic": _lib.BD_SPLIT_ATOMIC}
+
+
+def _p(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream=None):
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    s = stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+    return ctypes.c_void_p(s)
+
+
+def _need(t: torch.Tensor, dtype, what: str, numel: Optional[int] = None):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{what} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise TypeError(f"{what} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{what} must be contiguous")
+    if numel is not None and t.numel() < numel:
+        raise ValueError(f"{what} holds {t.numel()} elements, needs {numel}")
+
+
+def transcode(codes: torch.Tensor, scales: torch.Tensor, scale_block: int = 16,
+              e2m3: Optional[torch.Tensor] = None, e8m0: Optional[torch.Tensor] = None,
+              stream=None):
+    """NVFP4 -> MXFP6 (natural layouts). codes: packed nibbles (nblk*16 bytes); scales: E4M3
+    (nblk*2 bytes for scale_block 16, nblk for 32). Returns (e2m3 codes, e8m0)."""
+    if codes.numel() % 16:
+        raise ValueError("codes must hold a whole number of 32-element blocks (16 bytes each)")
+    nblk = codes.numel() // 16
+    _need(codes, torch.uint8, "codes")
+    _need(scales, torch.uint8, "scales", nblk * (2 if scale_block == 16 else 1))
+    if e2m3 is None:
+        e2m3 = torch.empty(nblk * 32, dtype=torch.uint8, device=codes.device)
+    if e8m0 is None:
+        e8m0 = torch.empty(nblk, dtype=torch.uint8, device=codes.device)
+    _need(e2m3, torch.uint8, "e2m3", nblk * 32)
+    _need(e8m0, torch.uint8, "e8m0", nblk)
+    call("bd_transcode_nvfp4_to_mxfp6", _p(codes), _p(scales), _p(e2m3), _p(e8m0), nblk,
+         scale_block, _stream(stream))
+    return e2m3, e8m0
+
+
+@dataclass
+class PackedWeights:
+    """NVFP4 weights in the GEMM's tiled layout (per-16 E4M3 scales + fp32 tensor scale)."""
+    codes: torch.Tensor    # [N/128][K/128][128][64] u8 (flat)
+    scales: torch.Tensor   # [N/128][K/128][128][8]  u8 (flat)
+    tensor_scale: float
+    N: int
+    K: int
+
+
+@dataclass
+class PackedActivations:
+    """MXFP6 activations in the GEMM operand layout."""
+    codes: torch.Tensor    # (M, K) u8, 12 packed bytes + 4 pad per 16 codes
+    scales: torch.Tensor   # [K/128][Mp4][4] E8M0 (flat)
+    M: int
+    K: int
+
+
+def pack_weights(codes: torch.Tensor, scales16: torch.Tensor, tensor_scale: float = 1.0,
+                 stream=None) -> PackedWeights:
+    """codes (N, K/2) packed nibbles, scales16 (N, K/16) E4M3 -> PackedWeights."""
+    N, Kh = codes.shape
+    K = Kh * 2
+    _need(codes, torch.uint8, "codes")
+    _need(scales16, torch.uint8, "scales16", N * K // 16)
+    tc = torch.empty(N * K // 2, dtype=torch.uint8, device=codes.device)
+    ts = torch.empty(N * K // 16, dtype=torch.uint8, device=codes.device)
+    call("bd_pack_b", _p(codes), _p(scales16), _p(tc), _p(ts), N, K, _stream(stream))
+    return PackedWeights(tc, ts, float(tensor_scale), N, K)
+
+
+def pack_activations(codes: torch.Tensor, e8m0: torch.Tensor, stream=None) -> PackedActivations:
+    """codes (M, K) one E2M3 code per byte, e8m0 (M, K/32) -> PackedActivations."""
+    M, K = codes.shape
+    _need(codes, torch.uint8, "codes")
+    _need(e8m0, torch.uint8, "e8m0", M * K // 32)
+    mp4 = (M + 3) // 4 * 4
+    out = torch.empty((M, K), dtype=torch.uint8, device=codes.device)
+    sc = torch.empty((K // 32) * mp4, dtype=torch.uint8, device=codes.device)
+    call("bd_pack_a", _p(codes), _p(e8m0), _p(out), _p(sc), M, K, _stream(stream))
+    return PackedActivations(out, sc, M, K)
+
+
+def query_workspace(M: int, N: int, K: int, split_k: int = 0, split_mode: str = "reduce") -> int:
+    return int(_lib.load().bd_query_workspace(M, N, K, split_k, SPLIT_MODES[split_mode]))
+
+
+def choose_split_k(M: int, N: int, K: int) -> int:
+    s = int(_lib.load().bd_choose_split_k(M, N, K))
+    _lib.check("bd_choose_split_k", min(s, 0))
+    return s
+
+
+def w4a6_gemm(acts: PackedActivations, weights: PackedWeights,
+              bias: Optional[torch.Tensor] = None, out_dtype=torch.bfloat16,
+              epilogue: str = "none", split_k: int = 0, split_mode: str = "reduce",
+              out: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
+              stream=None) -> torch.Tensor:
+    """C[M, N] = A . B^T * tensor_scale (+ bias, activation) on the tensor cores."""
+    M, K, N = acts.M, acts.K, weights.N
+    if weights.K != K:
+        raise ValueError(f"K mismatch: activations {K}, weights {weights.K}")
+    if split_k == 0:
+        split_k = choose_split_k(M, N, K)
+    planes = split_k if (split_mode == "planes" and split_k > 1) else 1
+    if out is None:
+        shape = (planes, M, N) if planes > 1 else (M, N)
+        alloc = torch.zeros if split_mode == "atomic" else torch.empty
+        out = alloc(shape, dtype=out_dtype, device=acts.codes.device)
+    _need(out, out_dtype, "out", planes * M * N)
+    ws_bytes = query_workspace(M, N, K, split_k, split_mode)
+    if ws_bytes and workspace is None:
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=acts.codes.device)
+    if bias is not None:
+        _need(bias, torch.bfloat16, "bias", N)
+    epi = EPILOGUES[epilogue]
+    if epi != _lib.BD_EPI_NONE and bias is None:
+        raise ValueError(f"epilogue {epilogue!r} needs a bias")
+    call("bd_w4a6_gemm", _p(out), _p(acts.codes), _p(acts.scales), _p(weights.codes),
+         _p(weights.scales), float(weights.tensor_scale), _p(bias), M, N, K, split_k,
+         SPLIT_MODES[split_mode], _OUT[out_dtype], epi, _p(workspace),
+         0 if workspace is None else workspace.numel() * workspace.element_size(),
+         _stream(stream))
+    return out
+
+
+def device_error(clear: bool = True) -> int:
+    """Error word set by kernels whose bounded waits ran out (0 = none)."""
+    w = ctypes.c_uint32(0)
+    call("bd_device_error", ctypes.byref(w), 1 if clear else 0)
+    return int(w.value)

@@ -1,0 +1,136 @@
+/*
+ * bitdance_b200.h -- C ABI of the B200 (sm_100a) W4A6 GEMM with on-chip NVFP4 -> MXFP6
+ * weight transcode.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream (passed as
+ * `bd_stream_t`, i.e. a `cudaStream_t` cast to `void*`; NULL = legacy default stream),
+ * enqueues work on that stream and returns a status code (BD_OK == 0, negative on error)
+ * without synchronising. Arguments are validated before anything is launched. No entry
+ * point allocates device memory; the caller owns every buffer.
+ *
+ * Data formats (all buffers are device memory, row-major unless stated):
+ *   NVFP4 weights B, "natural" layout:  codes (N, K/2) u8, element 2j in the low nibble of
+ *       byte j (E2M1 nibble = sign<<3 | magnitude index); scales (N, K/16) E4M3 bytes (or
+ *       (N, K/32) when scale_block == 32); one fp32 tensor scale.
+ *   NVFP4 weights B, "tiled" layout used by the GEMM (bd_pack_b produces it):
+ *       codes  [N/128][K/128][128 rows][64 bytes]   (same bytes, regrouped)
+ *       scales [N/128][K/128][128 rows][8 bytes]
+ *   MXFP6 activations A (bd_pack_a produces both from natural codes and scales):
+ *       codes  (M, K) u8: every 16 consecutive K-elements occupy 16 bytes, the first 12
+ *              holding the 16 six-bit E2M3 codes packed little-endian (code i at bits
+ *              6i..6i+5), the last 4 bytes padding. This is the tensor-core operand image.
+ *       scales [K/128][Mp4][4] E8M0 bytes, Mp4 = M rounded up to a multiple of 4.
+ *   MXFP6 codes in "natural" form (transcode output, bd_pack_a input): one E2M3 code per
+ *       byte in bits [5:0] (sign<<5 | exp<<3 | mantissa); E8M0 = exponent + 127.
+ */
+#ifndef BITDANCE_B200_H_
+#define BITDANCE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* bd_stream_t;
+
+/* ---- status codes ------------------------------------------------------------------- */
+#define BD_OK 0
+#define BD_ERR_INVALID_ARG (-1)  /* null pointer, bad enum value                          */
+#define BD_ERR_SHAPE (-2)        /* dimensions not supported (see each entry point)        */
+#define BD_ERR_ALIGNMENT (-3)    /* pointer misaligned for the vector/TMA access it needs  */
+#define BD_ERR_ARCH (-4)         /* current device is not sm_100 (B200)                    */
+#define BD_ERR_CUDA (-5)         /* a CUDA runtime call failed (launch error, ...)         */
+#define BD_ERR_WORKSPACE (-6)    /* workspace missing or smaller than bd_query_workspace() */
+#define BD_ERR_DEVICE (-7)       /* a kernel reported an error (bounded wait ran out)      */
+
+/* ---- GEMM options --------------------------------------------------------------------- */
+#define BD_OUT_BF16 0
+#define BD_OUT_F16 1
+#define BD_OUT_F32 2
+
+#define BD_EPI_NONE 0
+#define BD_EPI_BIAS 1
+#define BD_EPI_BIAS_RELU 2
+#define BD_EPI_BIAS_SILU 3
+#define BD_EPI_BIAS_GELU 4
+
+/* How split-K partial sums are combined (split_k > 1):
+ *   BD_SPLIT_REDUCE: fp32 partials in the caller's workspace, then a reduction kernel
+ *                    writes C (epilogue applied once, to the full sum).
+ *   BD_SPLIT_PLANES: partial plane z is written to c + z*M*N (out dtype); the caller sums.
+ *                    Replaces psg_preshuffle_gemm.py split_reduce="planes" (:296-331).
+ *   BD_SPLIT_ATOMIC: every split adds its fp32 partial into c (BD_OUT_F32 only, no
+ *                    epilogue, c zeroed by the caller; also at split_k == 1).
+ *                    Replaces split_reduce="atomic" (psg:2395-2410).                    */
+#define BD_SPLIT_REDUCE 0
+#define BD_SPLIT_PLANES 1
+#define BD_SPLIT_ATOMIC 2
+
+/* Library version (major*10000 + minor*100 + patch). */
+int bd_version(void);
+
+/* Human-readable text of a status code. */
+const char* bd_status_string(int status);
+
+/* Reads (and, if clear != 0, resets) the error word that kernels of this library set on
+ * the current device when a bounded wait runs out. Synchronises the device. Returns BD_OK
+ * and stores the word (0 = no error) in *word. */
+int bd_device_error(uint32_t* word, int clear);
+
+/* NVFP4 -> MXFP6 transcode, global -> global, natural layouts.
+ * nblk32 blocks of 32 elements: codes 16 B per block, scales 2 B per block (scale_block 16,
+ * the per-16 pair rule) or 1 B per block (scale_block 32), output 32 E2M3 code bytes and one
+ * E8M0 byte per block.
+ * Replaces the reference's golden_mxfp6 (kernel/nvfp4_codec.py:66-76) and its device forms
+ * _tc_bdata_fp4_to_fp6 / _tc_bscale_e4m3_to_e8m0 (psg_preshuffle_gemm.py:1154-1188,
+ * 1283-1329). Alignment: codes and e2m3_out 16 B, scales 2 B when scale_block == 16. */
+int bd_transcode_nvfp4_to_mxfp6(const uint8_t* codes, const uint8_t* scales, uint8_t* e2m3_out,
+                                uint8_t* e8m0_out, int64_t nblk32, int scale_block,
+                                bd_stream_t stream);
+
+/* Natural NVFP4 B -> tiled GEMM layout. N % 128 == 0, K % 128 == 0.
+ * Replaces the reference's host-side B pre-pack build_Bpk (kernel/hip/w4a6_tc_gemm_v31.hip:617-642)
+ * and the preshuffle B layout (ref_aiter_flydsl/mfma_preshuffle_pipeline.py:168-231). */
+int bd_pack_b(const uint8_t* codes, const uint8_t* scales16, uint8_t* codes_tiled,
+              uint8_t* scales_tiled, int N, int K, bd_stream_t stream);
+
+/* Natural MXFP6 A (one code per byte, (M, K/32) E8M0) -> GEMM operand layout. K % 128 == 0.
+ * scales_tiled must hold K/32 * Mp4 bytes; padding rows are written as 127 (2^0).
+ * Replaces the reference's A packing (pack6_block, kernel/verify_w4a6.py:55-59;
+ * build_Afrag, kernel/hip/w4a6_tc_gemm_v31.hip:608-615). */
+int bd_pack_a(const uint8_t* codes, const uint8_t* e8m0, uint8_t* a_packed,
+              uint8_t* scales_tiled, int M, int K, bd_stream_t stream);
+
+/* Bytes of workspace bd_w4a6_gemm needs for this problem (0 when split_k resolves to 1 or the
+ * split mode needs none). split_k == 0 means "let the library choose". */
+size_t bd_query_workspace(int M, int N, int K, int split_k, int split_mode);
+
+/* The split_k the library would use for split_k == 0 (auto). */
+int bd_choose_split_k(int M, int N, int K);
+
+/* C[M,N] = (A . B^T) * b_tensor_scale (+ bias[N], activation), fp32 accumulation.
+ * A: MXFP6 (bd_pack_a layout); B: NVFP4 (bd_pack_b tiled layout), transcoded on chip to MXFP6
+ * per the reference contract and fed to block-scaled tcgen05 MMAs.
+ * Shapes: M >= 1, N % 128 == 0, K % 128 == 0, (K/128) % split_k == 0.
+ * bias: N bf16 values (used when epilogue != BD_EPI_NONE). With split_mode PLANES, c holds
+ * split_k planes; with ATOMIC, out_dtype must be BD_OUT_F32 and epilogue BD_EPI_NONE.
+ * Replaces compile_preshuffle_gemm_a8(in_dtype="w4a6_tc") + launch_fn
+ * (psg_preshuffle_gemm.py:251-277, 3211-3253) and the HIP kernel `kern`
+ * (kernel/hip/w4a6_tc_gemm_v31.hip:152-604). */
+int bd_w4a6_gemm(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8_t* b,
+                 const uint8_t* b_scales, float b_tensor_scale, const void* bias, int M, int N,
+                 int K, int split_k, int split_mode, int out_dtype, int epilogue,
+                 void* workspace, size_t workspace_bytes, bd_stream_t stream);
+
+/* Sum of split_k fp32 partial planes (split_k, M, N) -> C (out dtype), times b_tensor_scale,
+ * plus bias/activation. Replaces the torch.sum over planes in kernel/bench_sweep.py:141-142. */
+int bd_splitk_reduce(const float* partials, void* c, const void* bias, float b_tensor_scale,
+                     int M, int N, int split_k, int out_dtype, int epilogue, bd_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BITDANCE_B200_H_ */

@@ -1,0 +1,133 @@
+"""The C-ABI library: it loads, exports every entry point include/bitdance_b200.h declares,
+and rejects bad arguments before touching a device (no compute calls here). CPU only."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "bitdance_b200.h")
+
+
+def declared_functions():
+    txt = open(HEADER).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(bd_[a-z0-9_]+)\s*\(", txt)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from bitdance_b200 import build
+    build.build_library()
+    from bitdance_b200 import _lib
+    return _lib.load()
+
+
+def test_header_declares_the_entry_points():
+    fns = declared_functions()
+    for f in ("bd_transcode_nvfp4_to_mxfp6", "bd_w4a6_gemm", "bd_splitk_reduce", "bd_pack_b",
+              "bd_pack_a", "bd_query_workspace"):
+        assert f in fns
+
+
+def test_library_exports_every_declared_symbol(lib):
+    from bitdance_b200 import _lib
+    for f in declared_functions():
+        assert hasattr(lib, f), f"{f} missing from libbitdance_b200.so"
+        assert f in _lib.SIGNATURES, f"{f} has no ctypes signature"
+
+
+def test_version_and_status_text(lib):
+    assert lib.bd_version() >= 100
+    assert lib.bd_status_string(0) == b"ok"
+    assert b"shape" in lib.bd_status_string(-2)
+
+
+def test_gemm_rejects_bad_arguments_before_launch(lib):
+    P = ctypes.c_void_p
+    ok = P(4096)  # never dereferenced: validation fails first
+    g = lib.bd_w4a6_gemm
+    # null pointer
+    assert g(None, ok, ok, ok, ok, 1.0, None, 16, 128, 128, 1, 0, 0, 0, None, 0, None) == -1
+    # bad out dtype / epilogue / split mode
+    assert g(ok, ok, ok, ok, ok, 1.0, None, 16, 128, 128, 1, 0, 7, 0, None, 0, None) == -1
+    assert g(ok, ok, ok, ok, ok, 1.0, None, 16, 128, 128, 1, 0, 0, 9, None, 0, None) == -1
+    assert g(ok, ok, ok, ok, ok, 1.0, None, 16, 128, 128, 1, 5, 0, 0, None, 0, None) == -1
+    # bias epilogue without bias
+    assert g(ok, ok, ok, ok, ok, 1.0, None, 16, 128, 128, 1, 0, 0, 1, None, 0, None) == -1
+    # shapes: N % 128, K % 128, M <= 0
+    assert g(ok, ok, ok, ok, ok, 1.0, None, 16, 100, 128, 1, 0, 0, 0, None, 0, None) == -2
+    assert g(ok, ok, ok, ok, ok, 1.0, None, 16, 128, 96, 1, 0, 0, 0, None, 0, None) == -2
+    assert g(ok, ok, ok, ok, ok, 1.0, None, 0, 128, 128, 1, 0, 0, 0, None, 0, None) == -2
+    # misaligned operand
+    assert g(ok, P(4097), ok, ok, ok, 1.0, None, 16, 128, 128, 1, 0, 0, 0, None, 0, None) == -3
+
+
+def test_transcode_rejects_bad_arguments(lib):
+    P = ctypes.c_void_p
+    ok = P(4096)
+    t = lib.bd_transcode_nvfp4_to_mxfp6
+    assert t(ok, ok, ok, ok, 8, 24, None) == -1      # scale_block
+    assert t(ok, ok, ok, ok, -1, 16, None) == -2     # negative size
+    assert t(ok, ok, ok, ok, 0, 16, None) == 0       # empty input is a no-op
+    assert t(None, ok, ok, ok, 8, 16, None) == -1
+    assert t(P(4100), ok, ok, ok, 8, 16, None) == -3
+    assert t(ok, P(4097), ok, ok, 8, 16, None) == -3  # per-16 scales read as u16
+
+
+def test_pack_rejects_bad_shapes(lib):
+    P = ctypes.c_void_p
+    ok = P(4096)
+    assert lib.bd_pack_b(ok, ok, ok, ok, 100, 128, None) == -2
+    assert lib.bd_pack_a(ok, ok, ok, ok, 4, 100, None) == -2
+    assert lib.bd_splitk_reduce(ok, ok, None, 1.0, 4, 6, 2, 0, 0, None) == -2
+
+
+def test_workspace_query(lib):
+    assert lib.bd_query_workspace(64, 1024, 1024, 4, 0) == 4 * 64 * 1024 * 4
+    assert lib.bd_query_workspace(64, 1024, 1024, 4, 1) == 0   # planes need none
+    assert lib.bd_query_workspace(64, 1024, 1024, 1, 0) == 0
+    assert lib.bd_query_workspace(64, 1000, 1024, 4, 0) == 0   # invalid shape
+
+
+def test_split_choice_fills_the_machine(lib):
+    # 112 weight tiles on 148 SMs: the library splits K
+    s = lib.bd_choose_split_k(16, 14336, 4096)
+    assert s >= 2 and (4096 // 128) % s == 0
+    assert lib.bd_choose_split_k(8192, 14336, 4096) == 1
+
+
+def test_psg_shim_validation_matches_reference_errors():
+    from bitdance_b200.psg import compile_preshuffle_gemm_a8 as c
+    with pytest.raises(ValueError):
+        c(K=256, tile_m=128, tile_n=128, tile_k=128, in_dtype="nope")
+    with pytest.raises(NotImplementedError):
+        c(K=256, tile_m=128, tile_n=128, tile_k=128, in_dtype="fp8")
+    with pytest.raises(ValueError):
+        c(K=256, tile_m=128, tile_n=128, tile_k=128, in_dtype="w4a6_tc", out_dtype="fp32")
+    with pytest.raises(NotImplementedError):
+        c(K=256, tile_m=128, tile_n=128, tile_k=256, in_dtype="w4a6_tc")
+    with pytest.raises(ValueError):
+        c(K=256, tile_m=128, tile_n=128, tile_k=128, in_dtype="w4a6_tc", split_k=0)
+    with pytest.raises(ValueError):
+        c(K=384, tile_m=128, tile_n=128, tile_k=128, in_dtype="w4a6_tc", split_k=2)
+    with pytest.raises(ValueError):
+        c(K=256, tile_m=128, tile_n=128, tile_k=128, in_dtype="w4a6_tc", split_reduce="tree")
+    with pytest.raises(ValueError):
+        c(K=256, tile_m=128, tile_n=128, tile_k=128, in_dtype="w4a6_tc", split_reduce="atomic",
+          epilogue="bias")
+    with pytest.raises(NotImplementedError):
+        c(K=256, tile_m=128, tile_n=128, tile_k=128, in_dtype="w4a6_tc", use_hw_transcode=True)
+    # the alias resolves like the reference's (psg:341-342)
+    assert c(K=256, tile_m=128, tile_n=128, tile_k=128, in_dtype="w6a6_tc").K == 256
+
+
+def test_product_path_never_imports_the_oracle():
+    pkg = os.path.join(ROOT, "bitdance_b200")
+    for dirpath, _, files in os.walk(pkg):
+        for f in files:
+            if f.endswith(".py"):
+                txt = open(os.path.join(dirpath, f)).read()
+                assert "w4a6_oracle" not in txt and "oracle/" not in txt and "liborc" not in txt, f

@@ -1,0 +1,186 @@
+"""W4A6 GEMM on the GPU against the oracle's dequantise-then-matmul gold (fp64 accumulation):
+C = deq(A) . deq(transcode(B))^T * s_t, max-abs-rel error <= 1e-2,
+plus an elementwise bound at bf16 resolution that any layout error would break."""
+import numpy as np
+import pytest
+
+import w4a6_oracle as o
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+TOL_REL_LINF = 1e-2
+
+
+def dev(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def random_operands(M, N, K, seed, b_scale_lo=0x28, b_scale_hi=0x50, a_e8_lo=120, a_e8_hi=134):
+    rng = np.random.default_rng(seed)
+    a_codes = rng.integers(0, 64, (M, K), dtype=np.uint8)
+    a_e8 = rng.integers(a_e8_lo, a_e8_hi + 1, (M, K // 32), dtype=np.uint8)
+    b_packed = rng.integers(0, 256, (N, K // 2), dtype=np.uint8)
+    b_sc = rng.integers(b_scale_lo, b_scale_hi + 1, (N, K // 16), dtype=np.uint8)
+    return a_codes, a_e8, b_packed, b_sc
+
+
+def quantized_operands(M, N, K, a_seed, b_seed, b_kind="normal", b_std=0.02, outliers=False):
+    if b_kind == "normal":
+        w = o.gen_normal((N, K), b_std, b_seed)
+    else:
+        w = o.gen_student_t((N, K), b_std, b_seed)
+    x = o.gen_outlier_acts((M, K), a_seed) if outliers else o.gen_normal((M, K), 1.0, a_seed)
+    a_codes, a_e8 = o.quantize_a_mxfp6(x)
+    b_codes, b_sc, s_t = o.quantize_b_nvfp4(w, block=16)
+    return a_codes, a_e8, o.pack_nibbles(b_codes), b_sc, float(s_t)
+
+
+def gold(a_codes, a_e8, b_packed, b_sc, s_t, bias=None):
+    e6, e8 = o.transcode_b(b_packed, b_sc, 16)
+    C = o.gemm_gold(a_codes, a_e8, e6, e8, s_t, bias)
+    Cabs = o.gemm_gold(a_codes & 0x1F, a_e8, e6 & 0x1F, e8, abs(s_t))
+    return C, Cabs
+
+
+def run_gpu(a_codes, a_e8, b_packed, b_sc, s_t, **kw):
+    import bitdance_b200 as bd
+    acts = bd.pack_activations(dev(a_codes), dev(a_e8))
+    w = bd.pack_weights(dev(b_packed), dev(b_sc), s_t)
+    C = bd.w4a6_gemm(acts, w, **kw)
+    torch.cuda.synchronize()
+    assert bd.device_error() == 0
+    return C
+
+
+def check(C_gpu, C, Cabs, out_dtype=torch.bfloat16):
+    g = C_gpu.float().cpu().numpy().astype(np.float64)
+    assert np.isfinite(g).all()
+    assert np.abs(g).max() > 0, "kernel wrote no output"
+    assert o.rel_linf(C, g) <= TOL_REL_LINF
+    ulp = {torch.bfloat16: 2.0 ** -8, torch.float16: 2.0 ** -11, torch.float32: 2.0 ** -22}[out_dtype]
+    bound = ulp * np.abs(C) + 2.0 ** -20 * Cabs + 1e-30
+    bad = np.abs(g - C) > bound
+    assert not bad.any(), f"{bad.sum()} elements outside bound; first at {np.argwhere(bad)[0]}"
+
+
+@pytest.mark.parametrize("M", [1, 4, 16, 17, 32, 64, 100, 128, 200, 256, 300])
+def test_random_codes_token_tiles(M):
+    N, K = 256, 512
+    ops = random_operands(M, N, K, seed=M)
+    C, Cabs = gold(*ops, 0.37)
+    check(run_gpu(*ops, 0.37, split_k=1), C, Cabs)
+
+
+@pytest.mark.parametrize("K", [128, 256, 384, 1024, 2176])
+def test_k_lengths_shorter_and_longer_than_the_pipeline(K):
+    M, N = 24, 384
+    ops = random_operands(M, N, K, seed=K)
+    C, Cabs = gold(*ops, 1.0)
+    check(run_gpu(*ops, 1.0, split_k=1), C, Cabs)
+
+
+def test_full_range_scales_with_subnormals_and_large_exponent_gaps():
+    M, N, K = 48, 256, 1024
+    ops = random_operands(M, N, K, seed=9, b_scale_lo=0x01, b_scale_hi=0x7E, a_e8_lo=100,
+                          a_e8_hi=150)
+    C, Cabs = gold(*ops, 2.0 ** -10)
+    check(run_gpu(*ops, 2.0 ** -10, split_k=1), C, Cabs)
+
+
+@pytest.mark.parametrize("split_k,mode", [(2, "reduce"), (4, "reduce"), (8, "reduce"),
+                                          (4, "planes"), (4, "atomic"), (1, "atomic")])
+def test_split_k_modes(split_k, mode):
+    M, N, K = 20, 512, 1024
+    ops = random_operands(M, N, K, seed=11 + split_k)
+    C, Cabs = gold(*ops, 0.5)
+    out_dtype = torch.float32 if mode == "atomic" else torch.bfloat16
+    got = run_gpu(*ops, 0.5, split_k=split_k, split_mode=mode, out_dtype=out_dtype)
+    if mode == "planes":
+        assert got.shape == (split_k, M, N)
+        got = got.float().sum(0)
+        C_ok = o.rel_linf(C, got.cpu().numpy()) <= TOL_REL_LINF
+        assert C_ok
+        return
+    check(got, C, Cabs, out_dtype)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_output_dtypes(out_dtype):
+    M, N, K = 40, 256, 512
+    ops = random_operands(M, N, K, seed=21, b_scale_lo=0x20, b_scale_hi=0x38)
+    C, Cabs = gold(*ops, 0.01)
+    check(run_gpu(*ops, 0.01, split_k=1, out_dtype=out_dtype), C, Cabs, out_dtype)
+
+
+@pytest.mark.parametrize("epi", ["bias", "bias_relu", "bias_silu", "bias_gelu"])
+@pytest.mark.parametrize("split_k", [1, 4])
+def test_epilogues(epi, split_k):
+    M, N, K = 33, 256, 1024
+    ops = random_operands(M, N, K, seed=31, b_scale_lo=0x18, b_scale_hi=0x30)
+    bias = (np.random.default_rng(5).standard_normal(N) * 4).astype(np.float32)
+    bias_bf = torch.from_numpy(bias).to(torch.bfloat16)
+    b64 = bias_bf.float().numpy().astype(np.float64)
+    C, Cabs = gold(*ops, 0.05, b64)
+    if epi == "bias_relu":
+        C = np.maximum(C, 0)
+    elif epi == "bias_silu":
+        C = C / (1 + np.exp(-C))
+    elif epi == "bias_gelu":
+        C = 0.5 * C * (1 + np.tanh(np.sqrt(2 / np.pi) * (C + 0.044715 * C ** 3)))
+    got = run_gpu(*ops, 0.05, split_k=split_k, bias=bias_bf.cuda(), epilogue=epi)
+    g = got.float().cpu().numpy()
+    assert o.rel_linf(C, g) <= TOL_REL_LINF
+    assert np.abs(g - C).max() <= 2.0 ** -7 * np.abs(C).max() + 1e-3
+
+
+def test_config1_quantized_normal():
+    """M=128, N=4096, K=4096; A ~ N(0,1) seed 0 -> MXFP6, B ~ N(0,0.02)
+    seed 1 -> NVFP4 per-16 + fp32 tensor scale."""
+    a_codes, a_e8, b_packed, b_sc, s_t = quantized_operands(128, 4096, 4096, 0, 1)
+    C, Cabs = gold(a_codes, a_e8, b_packed, b_sc, s_t)
+    check(run_gpu(a_codes, a_e8, b_packed, b_sc, s_t), C, Cabs)
+
+
+@pytest.mark.parametrize("M", [1, 4, 16, 32, 64])
+def test_config2_decode_shapes(M):
+    """BASELINE config 2 distributions (Student-t weights, outlier activations), N reduced to
+    2048 for the oracle; K = 4096 as in the config; library-chosen split-K."""
+    a_codes, a_e8, b_packed, b_sc, s_t = quantized_operands(M, 2048, 4096, 3 + M, 2,
+                                                            b_kind="t", outliers=True)
+    C, Cabs = gold(a_codes, a_e8, b_packed, b_sc, s_t)
+    check(run_gpu(a_codes, a_e8, b_packed, b_sc, s_t, split_k=0), C, Cabs)
+
+
+def test_verify_w4a6_constant_operands():
+    """kernel/verify_w4a6.py: constant-along-K operands give C = K * a * b * b_scale
+    (:122-193); byte-uniform A 0x55 decodes to +3.25 in every 6-bit slot (:81-97)."""
+    import bitdance_b200 as bd
+    M, N, K = 128, 256, 2048
+    a = torch.full((M, K), 0x55, dtype=torch.uint8, device="cuda")   # already operand layout
+    a_sc = torch.full(((K // 32) * M,), 127, dtype=torch.uint8, device="cuda")
+    acts = bd.PackedActivations(a, a_sc, M, K)
+    bc = o.E2M1_POS.tolist().index(2.0)
+    for b_scale, byte in ((1.0, 0x38), (1.5, 0x3C), (0.5, 0x30)):
+        w = bd.pack_weights(torch.full((N, K // 2), (bc << 4) | bc, dtype=torch.uint8, device="cuda"),
+                            torch.full((N, K // 16), byte, dtype=torch.uint8, device="cuda"), 1.0)
+        C = bd.w4a6_gemm(acts, w, split_k=1).float().cpu().numpy()
+        # the transcode folds the scale mantissa: 1.5 * 2 = 3 -> E2M3 1.5 * 2^1 exactly
+        expected = K * 3.25 * 2.0 * b_scale
+        assert np.all(np.abs(C - expected) <= 1e-3 * abs(expected)), (b_scale, C[:2, :3])
+
+
+def test_rejects_unsupported_shapes_and_small_workspace():
+    import bitdance_b200 as bd
+    from bitdance_b200 import BitdanceError, _lib
+    ops = random_operands(16, 256, 512, seed=1)
+    acts = bd.pack_activations(dev(ops[0]), dev(ops[1]))
+    w = bd.pack_weights(dev(ops[2]), dev(ops[3]), 1.0)
+    ws = torch.empty(16, dtype=torch.uint8, device="cuda")
+    with pytest.raises(BitdanceError) as e:
+        bd.w4a6_gemm(acts, w, split_k=4, split_mode="reduce", workspace=ws)
+    assert e.value.status == _lib.BD_ERR_WORKSPACE
+    with pytest.raises(BitdanceError) as e:
+        bd.w4a6_gemm(acts, w, split_k=3)
+    assert e.value.status == _lib.BD_ERR_SHAPE
