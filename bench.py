@@ -216,10 +216,9 @@ def run_ours(args, rank, world, local_rank):
     nat = {M: (rand_u8((M, K_W), 0, 64), rand_u8((M, K_W // 32), 120, 135)) for M in M_SWEEP}
     acts = {M: ops.pack_activations(*nat[M]) for M in M_SWEEP}
     outs = {M: torch.empty((M, N_W), dtype=torch.bfloat16, device=dev) for M in M_SWEEP}
-    splits = {M: ops.choose_split_k(M, N_W, K_W) for M in M_SWEEP}
-    wss = {M: torch.empty(max(16, ops.query_workspace(M, N_W, K_W, splits[M])), dtype=torch.uint8,
-                          device=dev) for M in M_SWEEP}
-    launches_per_step = sum(LAYERS * (2 if splits[M] > 1 else 1) for M in M_SWEEP)
+    splits = {M: 0 for M in M_SWEEP}   # 0 = persistent stream-K schedule
+    wss = {M: ops.Workspace() for M in M_SWEEP}
+    launches_per_step = len(M_SWEEP) * LAYERS
 
     # no-output guard (kernel/bench_sweep.py:297-326): a launch must write C
     for M in M_SWEEP:
@@ -275,8 +274,9 @@ def run_ours(args, rank, world, local_rank):
     g_e = capture(step_e2e)
 
     def timed(graph, steps, warmup, clocks=None):
-        for _ in range(warmup):
-            graph.replay()
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                graph.replay()
         torch.cuda.synchronize()
         if world > 1:
             torch.distributed.barrier()
@@ -285,10 +285,11 @@ def run_ours(args, rank, world, local_rank):
             clocks.start()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        for _ in range(steps):
-            graph.replay()
-        t1.record(stream)
+        with torch.cuda.stream(stream):
+            t0.record(stream)
+            for _ in range(steps):
+                graph.replay()
+            t1.record(stream)
         torch.cuda.synchronize()
         clk = clocks.summary() if clocks is not None else None
         if world > 1:
@@ -327,7 +328,7 @@ def run_ours(args, rank, world, local_rank):
         "data": "synthetic (uniform random E2M1 codes and E4M3 scale bytes; timing is value-independent)",
         "config": {"workload": f"decode sweep N={N_W} K={K_W} M in {list(M_SWEEP)} x {LAYERS} layers",
                    "per_rank_N": N_W, "global_N": N_W * world, "K": K_W,
-                   "split_k": {str(M): splits[M] for M in M_SWEEP},
+                   "schedule": "persistent stream-K (tiles split across CTAs finished in-kernel)",
                    "l2": f"{LAYERS} weight matrices per rank ({LAYERS * weight_bytes(N_W, K_W) / 1e6:.0f} MB) "
                          "rotate, larger than the 126 MB L2",
                    "parallelism": f"N-sharded x{world}, no collective in the timed region",
@@ -369,15 +370,16 @@ def prefill_bench(torch, ops, dev, g, peaks):
                                  torch.randint(120, 135, (M, K // 32), dtype=torch.uint8,
                                                device=dev, generator=g))
         out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        wsp = ops.Workspace()
         for _ in range(3):
-            ops.w4a6_gemm(a, w, out=out, split_k=1)
+            ops.w4a6_gemm(a, w, out=out, workspace=wsp)
         torch.cuda.synchronize()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         it = 10
         t0.record()
         for _ in range(it):
-            ops.w4a6_gemm(a, w, out=out, split_k=1)
+            ops.w4a6_gemm(a, w, out=out, workspace=wsp)
         t1.record()
         torch.cuda.synchronize()
         ms = t0.elapsed_time(t1) / it
@@ -387,8 +389,73 @@ def prefill_bench(torch, ops, dev, g, peaks):
     return res
 
 
+def run_case(args):
+    """One kernel shape, repeated: `--case gemm` (a single W4A6 GEMM) or `--case transcode`
+    (the standalone NVFP4 -> MXFP6 transcode of config 5). Prints its own JSON line; used for
+    Nsight Compute captures of one launch."""
+    import torch
+    import bitdance_b200 as bd
+    from bitdance_b200 import ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    if args.case == "gemm":
+        M, N, K = args.M, args.N, args.K
+        w = ops.pack_weights(torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev,
+                                           generator=g),
+                             torch.randint(0x58, 0x7F, (N, K // 16), dtype=torch.uint8,
+                                           device=dev, generator=g), 1.0)
+        a = ops.pack_activations(torch.randint(0, 64, (M, K), dtype=torch.uint8, device=dev,
+                                               generator=g),
+                                 torch.randint(120, 135, (M, K // 32), dtype=torch.uint8,
+                                               device=dev, generator=g))
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        split = args.split
+        wsp = ops.Workspace()
+        fn = lambda: ops.w4a6_gemm(a, w, out=out, split_k=split, workspace=wsp)  # noqa: E731
+        work = {"M": M, "N": N, "K": K, "split_k": split,
+                "weight_bytes": weight_bytes(N, K), "flops": 2 * M * N * K}
+    else:
+        nblk = args.nblk
+        codes = torch.randint(0, 256, (nblk * 16,), dtype=torch.uint8, device=dev, generator=g)
+        sc = torch.randint(0x01, 0x7F, (nblk * 2,), dtype=torch.uint8, device=dev, generator=g)
+        e6 = torch.empty(nblk * 32, dtype=torch.uint8, device=dev)
+        e8 = torch.empty(nblk, dtype=torch.uint8, device=dev)
+        fn = lambda: ops.transcode(codes, sc, 16, e2m3=e6, e8m0=e8)  # noqa: E731
+        work = {"nblk32": nblk, "bytes": nblk * (16 + 2 + 32 + 1)}
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        fn()
+    t1.record()
+    torch.cuda.synchronize()
+    us = t0.elapsed_time(t1) * 1e3 / args.steps
+    res = {"case": args.case, "us_per_call": us, **work}
+    if args.case == "gemm":
+        res["weight_gbs"] = work["weight_bytes"] / us / 1e3
+        res["tflops"] = work["flops"] / us / 1e6
+    else:
+        res["gbs"] = work["bytes"] / us / 1e3
+    if bd.device_error() != 0:
+        raise RuntimeError("kernel error word set")
+    print(json.dumps(res), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--case", choices=["gemm", "transcode"], default=None,
+                    help="time one kernel shape instead of the benchmark step")
+    ap.add_argument("--M", type=int, default=16)
+    ap.add_argument("--N", type=int, default=14336)
+    ap.add_argument("--K", type=int, default=4096)
+    ap.add_argument("--split", type=int, default=0)
+    ap.add_argument("--nblk", type=int, default=1 << 26)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
@@ -399,6 +466,8 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.case:
+        return run_case(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -5,7 +5,7 @@ The compute lives in ``libbitdance_b200.so`` (C ABI: include/bitdance_b200.h); t
 is its Python host side. ``psg`` mirrors the reference operator ``compile_preshuffle_gemm_a8``.
 """
 from ._lib import BitdanceError, load  # noqa: F401
-from .ops import (PackedActivations, PackedWeights, choose_split_k, device_error,  # noqa: F401
+from .ops import (PackedActivations, PackedWeights, Workspace, device_error,  # noqa: F401
                   pack_activations, pack_weights, query_workspace, transcode, w4a6_gemm)
 
 __version__ = "0.1.0"

@@ -40,7 +40,6 @@ SIGNATURES = {
     "bd_pack_b": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "bd_pack_a": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "bd_query_workspace": (_SZ, [_I, _I, _I, _I, _I]),
-    "bd_choose_split_k": (_I, [_I, _I, _I]),
     "bd_w4a6_gemm": (_I, [_P, _P, _P, _P, _P, _F, _P, _I, _I, _I, _I, _I, _I, _I, _P, _SZ, _P]),
     "bd_splitk_reduce": (_I, [_P, _P, _P, _F, _I, _I, _I, _I, _I, _P]),
 }

@@ -105,31 +105,27 @@ int token_tile(int M) {
   return 256;
 }
 
-int choose_split(int M, int N, int K, int sm_count) {
-  const int nkt = K / 128;
+// Stream-K scratch of one call: per-CTA partial slots [grid][2][BN][128] fp32, then one
+// arrival counter per tile. Counters must be zero before the first call; every call leaves
+// them zero again.
+struct StreamKSizes {
+  size_t slots_bytes, counter_bytes, total;
+};
+StreamKSizes streamk_sizes(int M, int N, int K, int sm_count) {
   const int bn = token_tile(M);
   const int64_t tiles = static_cast<int64_t>(N / 128) * ((M + bn - 1) / bn);
-  if (tiles >= sm_count) return 1;
-  int best = 1;
-  double best_score = 0.0;
-  for (int s = 1; s <= nkt; ++s) {
-    if (nkt % s) continue;
-    if (s > 1 && nkt / s < 4) break;
-    const int64_t ctas = tiles * s;
-    const int64_t waves = (ctas + sm_count - 1) / sm_count;
-    double score = static_cast<double>(ctas) / static_cast<double>(waves * sm_count);
-    score -= 0.02 * (s > 1 ? 1 : 0);  // the reduction pass is not free
-    if (score > best_score + 1e-9) {
-      best_score = score;
-      best = s;
-    }
-  }
-  return best;
+  const int64_t units = tiles * (K / 128);
+  const int64_t grid = units < sm_count ? units : sm_count;
+  StreamKSizes z;
+  z.slots_bytes = (static_cast<size_t>(grid) * 2 * bn * 128 * sizeof(float) + 255) / 256 * 256;
+  z.counter_bytes = (static_cast<size_t>(tiles) * sizeof(uint32_t) + 255) / 256 * 256;
+  z.total = z.slots_bytes + z.counter_bytes;
+  return z;
 }
 
 template <int BN>
-int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tas, const GemmParams& p, int M,
-                   int N, int split, cudaStream_t stream) {
+int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tas, const CUtensorMap& tw,
+                   const GemmParams& p, int grid, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
@@ -141,8 +137,7 @@ int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tas, const GemmPara
       return BD_ERR_CUDA;
     configured.fetch_or(bit);
   }
-  const dim3 grid(N / 128, (M + BN - 1) / BN, split);
-  w4a6_gemm_kernel<BN><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tas, p);
+  w4a6_gemm_kernel<BN><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tas, tw, p);
   return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
 }
 
@@ -241,17 +236,14 @@ int bd_pack_a(const uint8_t* codes, const uint8_t* e8m0, uint8_t* a_packed, uint
   return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
 }
 
-int bd_choose_split_k(int M, int N, int K) {
-  if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % 128) return BD_ERR_SHAPE;
-  DeviceInfo* d = nullptr;
-  int st = device_info(&d);
-  const int sms = (st == BD_OK || st == BD_ERR_ARCH) && d ? d->sm_count : 148;
-  return choose_split(M, N, K, sms > 0 ? sms : 148);
-}
-
 size_t bd_query_workspace(int M, int N, int K, int split_k, int split_mode) {
-  if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % 128) return 0;
-  if (split_k == 0) split_k = bd_choose_split_k(M, N, K);
+  if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % 128 || split_k < 0) return 0;
+  if (split_k == 0) {
+    DeviceInfo* d = nullptr;
+    const int st = device_info(&d);
+    const int sms = (st == BD_OK || st == BD_ERR_ARCH) && d ? d->sm_count : 148;
+    return streamk_sizes(M, N, K, sms > 0 ? sms : 148).total;
+  }
   if (split_k <= 1 || split_mode != BD_SPLIT_REDUCE) return 0;
   return static_cast<size_t>(split_k) * static_cast<size_t>(M) * static_cast<size_t>(N) *
          sizeof(float);
@@ -289,66 +281,84 @@ int bd_w4a6_gemm(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8
   if (!aligned(a, 16) || !aligned(a_scales, 16) || !aligned(b, 16) || !aligned(b_scales, 16) ||
       (bias && !aligned(bias, 2)))
     return BD_ERR_ALIGNMENT;
-  DeviceInfo* d = nullptr;
-  int st = device_info(&d);
-  if (st != BD_OK) return st;
   const int nkt = K / 128;
-  if (split_k == 0) split_k = choose_split(M, N, K, d->sm_count);
-  if (split_k < 1 || nkt % split_k) return BD_ERR_SHAPE;
+  if (split_k < 0 || (split_k > 0 && nkt % split_k)) return BD_ERR_SHAPE;
   if (split_mode == BD_SPLIT_ATOMIC && (out_dtype != BD_OUT_F32 || epilogue != BD_EPI_NONE))
     return BD_ERR_INVALID_ARG;
   if (split_k > 1 && split_mode == BD_SPLIT_PLANES && epilogue != BD_EPI_NONE)
     return BD_ERR_INVALID_ARG;
+  DeviceInfo* d = nullptr;
+  int st = device_info(&d);
+  if (st != BD_OK) return st;
+
+  const int bn = token_tile(M);
+  const int m_tiles = (M + bn - 1) / bn, n_tiles = N / 128;
+  const int64_t tiles = static_cast<int64_t>(m_tiles) * n_tiles;
+  // stream-K for split_k == 0 unless atomics are asked for (they need no fix-up)
+  const bool streamk = split_k == 0 && split_mode != BD_SPLIT_ATOMIC;
+  if (split_k == 0 && !streamk) split_k = 1;
   const bool use_ws = split_k > 1 && split_mode == BD_SPLIT_REDUCE;
+  StreamKSizes sk{0, 0, 0};
+  if (streamk) {
+    sk = streamk_sizes(M, N, K, d->sm_count);
+    if (!workspace || workspace_bytes < sk.total) return BD_ERR_WORKSPACE;
+    if (!aligned(workspace, 256)) return BD_ERR_ALIGNMENT;
+  }
   if (use_ws) {
     const size_t need = static_cast<size_t>(split_k) * M * static_cast<size_t>(N) * sizeof(float);
     if (!workspace || workspace_bytes < need) return BD_ERR_WORKSPACE;
     if (!aligned(workspace, 16) || N % 4) return BD_ERR_ALIGNMENT;
   }
 
-  const int bn = token_tile(M);
   const int Mp4 = (M + 3) / 4 * 4;
-  CUtensorMap ta, tas;
+  CUtensorMap ta, tas, tw;
   if (!make_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, const_cast<uint8_t*>(a), K, M, K, 128, bn,
                    CU_TENSOR_MAP_SWIZZLE_128B))
     return BD_ERR_CUDA;
   if (!make_map_2d(&tas, CU_TENSOR_MAP_DATA_TYPE_UINT32, const_cast<uint8_t*>(a_scales), Mp4,
                    nkt, static_cast<uint64_t>(Mp4) * 4, bn, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
     return BD_ERR_CUDA;
+  if (!make_map_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, const_cast<uint8_t*>(b), 64,
+                   static_cast<uint64_t>(N) * nkt, 64, 64, 128, CU_TENSOR_MAP_SWIZZLE_64B))
+    return BD_ERR_CUDA;
 
   GemmParams p;
-  p.wcodes = b;
   p.wscales = b_scales;
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.tensor_scale = b_tensor_scale;
   p.M = M;
   p.N = N;
   p.K = K;
-  p.ktiles = nkt / split_k;
+  p.n_tiles = n_tiles;
+  p.m_tiles = m_tiles;
+  p.nkt = nkt;
+  p.split_k = streamk ? 0 : split_k;
   p.out_dtype = out_dtype;
   p.epilogue = epilogue;
   p.err = d->err;
-  if (split_mode == BD_SPLIT_ATOMIC) {
-    p.out_mode = kOutAtomic;  // accumulates into c even at split_k == 1
-    p.out = c;
-  } else if (split_k == 1) {
-    p.out_mode = kOutC;
-    p.out = c;
-  } else if (split_mode == BD_SPLIT_REDUCE) {
-    p.out_mode = kOutPartial;
+  p.slots = nullptr;
+  p.counters = nullptr;
+  p.out = c;
+  if (split_mode == BD_SPLIT_ATOMIC) p.split_out = kOutAtomic;
+  else if (split_k <= 1) p.split_out = kOutC;
+  else if (split_mode == BD_SPLIT_REDUCE) {
+    p.split_out = kOutPartial;
     p.out = workspace;
-  } else {
-    p.out_mode = kOutPlane;
-    p.out = c;
+  } else p.split_out = kOutPlane;
+  int64_t work = streamk ? tiles * nkt : tiles * split_k;
+  if (streamk) {
+    p.slots = static_cast<float*>(workspace);
+    p.counters = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + sk.slots_bytes);
   }
+  const int grid = static_cast<int>(work < d->sm_count ? work : d->sm_count);
   cudaStream_t s = as_stream(stream);
   int rc;
   switch (bn) {
-    case 16: rc = launch_gemm_bn<16>(ta, tas, p, M, N, split_k, s); break;
-    case 32: rc = launch_gemm_bn<32>(ta, tas, p, M, N, split_k, s); break;
-    case 64: rc = launch_gemm_bn<64>(ta, tas, p, M, N, split_k, s); break;
-    case 128: rc = launch_gemm_bn<128>(ta, tas, p, M, N, split_k, s); break;
-    default: rc = launch_gemm_bn<256>(ta, tas, p, M, N, split_k, s); break;
+    case 16: rc = launch_gemm_bn<16>(ta, tas, tw, p, grid, s); break;
+    case 32: rc = launch_gemm_bn<32>(ta, tas, tw, p, grid, s); break;
+    case 64: rc = launch_gemm_bn<64>(ta, tas, tw, p, grid, s); break;
+    case 128: rc = launch_gemm_bn<128>(ta, tas, tw, p, grid, s); break;
+    default: rc = launch_gemm_bn<256>(ta, tas, tw, p, grid, s); break;
   }
   if (rc != BD_OK || !use_ws) return rc;
   return bd_splitk_reduce(static_cast<const float*>(workspace), c, bias, b_tensor_scale, M, N,

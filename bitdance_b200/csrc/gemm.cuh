@@ -1,21 +1,27 @@
 // gemm.cuh -- fused W4A6 GEMM for sm_100a: C = A_mxfp6 . transcode(B_nvfp4)^T.
 //
-// One CTA computes a 128 (weight rows, N) x BN (tokens, M) tile of C^T in tensor memory:
-// the weights are the MMA's M operand and the tokens its N operand, so a decode batch of a
-// few tokens still fills 128-row MMAs. Per 128-wide K chunk ("stage"):
+// Tiles of C^T: 128 weight rows (N, the MMA's M operand) x BN tokens (M, the MMA's N
+// operand), so a decode batch of a few tokens still fills 128-row MMAs.
 //
-//   warp 0      producer   bulk copies of the packed NVFP4 codes (8 KB) and E4M3 scales
-//                          (1 KB) from the tiled B layout, TMA tensor loads of the token
-//                          tile (128B-swizzled) and of its E8M0 scales; one mbarrier.
-//   warps 2..9  transcode  NVFP4 -> MXFP6 of the 128x128 weight chunk straight into the
-//                          128B-swizzled operand buffer (values as E4M3 bytes), the weight
-//                          E8M0 scales and the token scales into tcgen05.cp layout.
-//   warp 1      MMA        tcgen05.cp of both scale blocks to TMEM, 4 block-scaled
-//                          tcgen05.mma (kind::mxf8f6f4, K = 32 each), commit frees the stage.
-//   warps 2..9  epilogue   TMEM -> registers -> (x tensor scale, bias, activation) -> C.
+// Persistent CTAs walk a schedule of "segments" (a tile and a range of 128-wide K chunks):
+//   * stream-K (the default): the (tile, K chunk) units are cut into one contiguous range per
+//     CTA; a tile split between CTAs is finished in-kernel -- every contributor stores its
+//     fp32 partial in a per-CTA slot, the last one to arrive (atomic counter) sums the slots
+//     in CTA order and writes C, so results do not depend on timing;
+//   * explicit split-K (split_k >= 1): items (tile, split) dealt round-robin, written as
+//     partial planes, fp32 workspace planes or fp32 atomics (the reference's split modes).
 //
-// Split-K: blockIdx.z covers K/split_k; partial results go to the workspace, to planes of C
-// or are added atomically, as the host asks.
+// Warp roles (704 threads):
+//   warp 0      producer   TMA: packed NVFP4 codes (8 KB, 64B-swizzled), E4M3 scales (1 KB),
+//                          token tile (128B-swizzled), token E8M0 scales; one mbarrier/stage.
+//   warps 6..21 transcode  16 warps; warp (quarter q, K block j) turns rows 32q..32q+31 x
+//                          32 K-elements into E4M3 bytes in tensor memory (tcgen05.st; the
+//                          MMA reads its A operand from there) and their E8M0 scales.
+//   warp 1      MMA        tcgen05.cp of both scale blocks, 4 block-scaled tcgen05.mma
+//                          (kind::mxf8f6f4, A from TMEM, K = 32 each), commit frees the stage.
+//   warps 2..5  epilogue   TMEM accumulator -> registers -> C / partials (double-buffered
+//                          accumulators when tensor memory allows, so it overlaps the next
+//                          segment's main loop).
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -31,18 +37,6 @@ enum : int {
   kOutAtomic = 3,  // scaled partials added into fp32 C
 };
 
-struct GemmParams {
-  const uint8_t* wcodes;   // [N/128][K/128][128][64]
-  const uint8_t* wscales;  // [N/128][K/128][128][8]
-  void* out;               // C, or workspace for kOutPartial
-  const __nv_bfloat16* bias;
-  float tensor_scale;
-  int M, N, K;
-  int ktiles;              // 128-wide K chunks per split
-  int out_mode, out_dtype, epilogue;
-  uint32_t* err;
-};
-
 constexpr int cround(int x, int a) { return (x + a - 1) / a * a; }
 constexpr int cpow2(int x) {
   int p = 32;
@@ -52,39 +46,114 @@ constexpr int cpow2(int x) {
 
 template <int BN>
 struct GemmCfg {
-  static constexpr int kStages = BN >= 256 ? 3 : (BN >= 128 ? 5 : (BN >= 64 ? 6 : 7));
-  static constexpr int kW8 = 128 * 128;
-  static constexpr int kA = BN * 128;
-  static constexpr int kWCode = 128 * 64;
-  static constexpr int kWScale = 128 * 8;
-  static constexpr int kAScale = BN * 4;
+  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 5 : 8);
+  static constexpr int kTok = BN * 128;       // token tile (E2M3 operand image), SW128
+  static constexpr int kWCode = 128 * 64;     // packed NVFP4 codes, SW64
+  static constexpr int kWScale = 128 * 8;     // E4M3 per-16 scales
+  static constexpr int kTokScale = cround(BN * 4, 128);
   static constexpr int kSfA = BN > 128 ? 1024 : 512;
-  static constexpr int oW8 = 0;
-  static constexpr int oA = oW8 + kW8;
-  static constexpr int oWCode = oA + kA;
+  static constexpr int oTok = 0;
+  static constexpr int oWCode = cround(oTok + kTok, 1024);
   static constexpr int oWScale = oWCode + kWCode;
-  static constexpr int oAScale = oWScale + kWScale;
-  static constexpr int oSfW = cround(oAScale + kAScale, 128);
+  static constexpr int oTokScale = oWScale + kWScale;
+  static constexpr int oSfW = oTokScale + kTokScale;
   static constexpr int oSfA = oSfW + 512;
   static constexpr int kStageBytes = cround(oSfA + kSfA, 1024);
-  static constexpr int kTxBytes = kWCode + kWScale + kA + kAScale;
+  static constexpr int kTxBytes = kWCode + kWScale + kTok + BN * 4;
+  // tensor memory: accumulators, then per stage 32 columns of A (128 B of K per lane) and
+  // the scale factors (4 columns for the weights, 4 or 8 for the tokens)
   static constexpr int kSfCols = 4 + (BN > 128 ? 8 : 4);
-  static constexpr int kSfCol0 = BN < 32 ? 32 : BN;
+  static constexpr int kAccCols = BN < 32 ? 32 : BN;
+  static constexpr int kNumAcc = (2 * kAccCols + kStages * (32 + kSfCols) <= 512) ? 2 : 1;
+  static constexpr int kACol0 = kNumAcc * kAccCols;
+  static constexpr int kSfCol0 = kACol0 + kStages * 32;
   static constexpr int kTmemCols = cpow2(kSfCol0 + kStages * kSfCols);
-  // control block after the stages
   static constexpr int oCtl = kStages * kStageBytes;
-  static constexpr int kCtlBytes = 1024;
+  static constexpr int kCtlBytes = 2048;
   static constexpr int kSmemBytes = oCtl + kCtlBytes + 1024;  // + alignment slack
-  static constexpr int kThreads = 320;
+  static constexpr int kTranscodeWarps = 16;
+  static constexpr int kEpiWarps = 4;
+  static constexpr int kThreads = 32 * (2 + kEpiWarps + kTranscodeWarps);
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static_assert(kTmemCols <= 512, "tensor memory budget");
+  static_assert(kStages <= 8, "control block holds 8 stages");
 };
 
 struct GemmCtl {
-  uint64_t full[8], ready[8], empty[8], accum;
+  uint64_t full[8], ready[8], empty[8], acc_full[2], acc_empty[2], drain;
   uint32_t tmem_base;
   uint32_t abort_flag;
+  uint32_t bcast;
   TranscodeTables tab;
+};
+
+struct GemmParams {
+  const uint8_t* wscales;       // [N/128][K/128][128][8] (codes come through the tensor map)
+  void* out;                    // C, or the fp32 workspace planes (kOutPartial)
+  float* slots;                 // stream-K partial slots [grid][2][BN][128]
+  uint32_t* counters;           // stream-K per-tile arrival counters (zero between calls)
+  const __nv_bfloat16* bias;
+  float tensor_scale;
+  int M, N, K;
+  int n_tiles, m_tiles, nkt;
+  int split_k;                  // 0 = stream-K, else explicit split
+  int split_out;                // output mode of explicit split segments
+  int out_dtype, epilogue;
+  uint32_t* err;
+};
+
+// One contiguous run of K chunks of one tile.
+struct Seg {
+  int tile, kt0, kt1, z, slot;  // slot: -1 full tile, 0/1 stream-K partial slot
+};
+
+// The work of CTA `c` of `G`: segment number `idx` (false when there is none).
+struct Schedule {
+  int64_t U;    // units (tile, K chunk)
+  int64_t q, r; // stream-K: U = q*G + r
+  int G, nkt, tiles, split;
+
+  __device__ __forceinline__ void init(const GemmParams& p, int grid) {
+    G = grid;
+    nkt = p.nkt;
+    tiles = p.n_tiles * p.m_tiles;
+    split = p.split_k;
+    U = static_cast<int64_t>(tiles) * nkt;
+    q = U / G;
+    r = U % G;
+  }
+  __device__ __forceinline__ int64_t u0(int c) const {
+    return c * q + (static_cast<int64_t>(c) < r ? static_cast<int64_t>(c) : r);
+  }
+  __device__ __forceinline__ int cta_of(int64_t u) const {
+    const int64_t big = r * (q + 1);
+    return u < big ? static_cast<int>(u / (q + 1)) : static_cast<int>(r + (u - big) / q);
+  }
+  __device__ __forceinline__ bool segment(int c, int idx, Seg& s) const {
+    if (split > 0) {
+      const int64_t item = c + static_cast<int64_t>(idx) * G;
+      if (item >= static_cast<int64_t>(tiles) * split) return false;
+      s.tile = static_cast<int>(item / split);
+      s.z = static_cast<int>(item % split);
+      const int per = nkt / split;
+      s.kt0 = s.z * per;
+      s.kt1 = s.kt0 + per;
+      s.slot = -1;
+      return true;
+    }
+    const int64_t a = u0(c), b = u0(c + 1);
+    if (a >= b) return false;
+    const int64_t t = a / nkt + idx;
+    const int64_t lo = a > t * nkt ? a : t * nkt;
+    const int64_t hi = b < (t + 1) * nkt ? b : (t + 1) * nkt;
+    if (lo >= hi) return false;
+    s.tile = static_cast<int>(t);
+    s.kt0 = static_cast<int>(lo - t * nkt);
+    s.kt1 = static_cast<int>(hi - t * nkt);
+    s.z = 0;
+    s.slot = (s.kt0 == 0 && s.kt1 == nkt) ? -1 : (idx == 0 ? 0 : 1);
+    return true;
+  }
 };
 
 __device__ __forceinline__ float apply_epilogue(float v, int epi, const __nv_bfloat16* bias,
@@ -105,10 +174,32 @@ __device__ __forceinline__ void store_out(void* out, int64_t idx, float v, int d
   else reinterpret_cast<float*>(out)[idx] = v;
 }
 
+__device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Eight E2M1 nibbles (one word) -> eight E4M3 bytes (two words) with the magnitude table
+// T of the 16-block's class. Signs: byte i of (w<<4) / w carries the sign of element 2i /
+// 2i+1 in bit 7, so one prmt gathers four of them.
+__device__ __forceinline__ void nib8_to_e4m3(uint32_t w, uint2 T, uint32_t& lo, uint32_t& hi) {
+  const uint32_t m = w & 0x77777777u;
+  const uint32_t t = w << 4;
+  lo = (prmt(t, w, 0x5140u) & 0x80808080u) | prmt(T.x, T.y, m);
+  hi = (prmt(t, w, 0x7362u) & 0x80808080u) | prmt(T.x, T.y, m >> 16);
+}
+
 template <int BN>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
     w4a6_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
-                     const __grid_constant__ CUtensorMap tm_as, const GemmParams p) {
+                     const __grid_constant__ CUtensorMap tm_as,
+                     const __grid_constant__ CUtensorMap tm_w, const GemmParams p) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -116,26 +207,29 @@ __global__ void __launch_bounds__(320, 1)
   GemmCtl& ctl = *reinterpret_cast<GemmCtl*>(smem + Cfg::oCtl);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n_tile = blockIdx.x, m0 = blockIdx.y * BN, split = blockIdx.z;
-  const int n0 = n_tile * 128;
-  const int nkt_total = p.K / 128;
-  const int kt0 = split * p.ktiles;
-  const int nk = p.ktiles;
+  const int cta = blockIdx.x;
   volatile uint32_t* abort_flag = &ctl.abort_flag;
+  Schedule sch;
+  sch.init(p, gridDim.x);
 
   if (tid == 0) {
     ctl.abort_flag = 0;
     for (int s = 0; s < S; ++s) {
       mbar_init(smem_u32(&ctl.full[s]), 1);
-      mbar_init(smem_u32(&ctl.ready[s]), 8);
+      mbar_init(smem_u32(&ctl.ready[s]), Cfg::kTranscodeWarps);
       mbar_init(smem_u32(&ctl.empty[s]), 1);
     }
-    mbar_init(smem_u32(&ctl.accum), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&ctl.acc_full[b]), 1);
+      mbar_init(smem_u32(&ctl.acc_empty[b]), Cfg::kEpiWarps);
+    }
+    mbar_init(smem_u32(&ctl.drain), 1);
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm_a);
     prefetch_tmap(&tm_as);
+    prefetch_tmap(&tm_w);
   }
   load_tables<true>(ctl.tab, tid, Cfg::kThreads);
   if (warp == 1) {
@@ -150,123 +244,213 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
-      const uint8_t* wc = p.wcodes + (static_cast<int64_t>(n_tile) * nkt_total + kt0) * 8192;
-      const uint8_t* ws = p.wscales + (static_cast<int64_t>(n_tile) * nkt_total + kt0) * 1024;
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (i / S) & 1;
-        if (!mbar_wait(smem_u32(&ctl.empty[s]), ph ^ 1u, p.err, kErrWaitEmpty, abort_flag)) break;
-        uint8_t* st = smem + s * Cfg::kStageBytes;
-        const uint32_t fb = smem_u32(&ctl.full[s]);
-        mbar_arrive_expect_tx(fb, Cfg::kTxBytes);
-        bulk_load(smem_u32(st + Cfg::oWCode), wc + static_cast<int64_t>(i) * 8192, 8192, fb);
-        bulk_load(smem_u32(st + Cfg::oWScale), ws + static_cast<int64_t>(i) * 1024, 1024, fb);
-        tma_load_2d(smem_u32(st + Cfg::oA), &tm_a, (kt0 + i) * 128, m0, fb);
-        tma_load_2d(smem_u32(st + Cfg::oAScale), &tm_as, m0, kt0 + i, fb);
+      int i = 0;
+      Seg sg;
+      for (int idx = 0; sch.segment(cta, idx, sg) && !*abort_flag; ++idx) {
+        const int mt = sg.tile / p.n_tiles, nt = sg.tile % p.n_tiles;
+        for (int kt = sg.kt0; kt < sg.kt1; ++kt, ++i) {
+          const int s = i % S;
+          const uint32_t ph = (i / S) & 1;
+          if (!mbar_wait(smem_u32(&ctl.empty[s]), ph ^ 1u, p.err, kErrWaitEmpty, abort_flag)) break;
+          uint8_t* st = smem + s * Cfg::kStageBytes;
+          const uint32_t fb = smem_u32(&ctl.full[s]);
+          const int64_t chunk = static_cast<int64_t>(nt) * p.nkt + kt;
+          mbar_arrive_expect_tx(fb, Cfg::kTxBytes);
+          tma_load_2d(smem_u32(st + Cfg::oWCode), &tm_w, 0, static_cast<int32_t>(chunk * 128), fb);
+          bulk_load(smem_u32(st + Cfg::oWScale), p.wscales + chunk * 1024, 1024, fb);
+          tma_load_2d(smem_u32(st + Cfg::oTok), &tm_a, kt * 128, mt * BN, fb);
+          tma_load_2d(smem_u32(st + Cfg::oTokScale), &tm_as, mt * BN, kt, fb);
+        }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t tD = tbase;
-      for (int i = 0; i < nk; ++i) {
+      int i = 0;
+      Seg sg;
+      for (int idx = 0; sch.segment(cta, idx, sg); ++idx) {
+        const int buf = Cfg::kNumAcc == 2 ? (idx & 1) : 0;
+        const uint32_t use = Cfg::kNumAcc == 2 ? (idx >> 1) : idx;
+        if (!mbar_wait(smem_u32(&ctl.acc_empty[buf]), (use & 1) ^ 1u, p.err, kErrWaitAccum,
+                       abort_flag))
+          break;
+        tc_fence_after();
+        const uint32_t tD = tbase + buf * Cfg::kAccCols;
+        bool ok = true;
+        for (int kt = sg.kt0; kt < sg.kt1; ++kt, ++i) {
+          const int s = i % S;
+          const uint32_t ph = (i / S) & 1;
+          if (!mbar_wait(smem_u32(&ctl.ready[s]), ph, p.err, kErrWaitOperand, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint8_t* st = smem + s * Cfg::kStageBytes;
+          const uint32_t tSfW = tbase + Cfg::kSfCol0 + s * Cfg::kSfCols;
+          const uint32_t tSfA = tSfW + 4;
+          tmem_cp_32x128b_x4(tSfW, sdesc_plain(smem_u32(st + Cfg::oSfW), 0, 128));
+          tmem_cp_32x128b_x4(tSfA, sdesc_plain(smem_u32(st + Cfg::oSfA), 0, 128));
+          if constexpr (BN > 128)
+            tmem_cp_32x128b_x4(tSfA + 4, sdesc_plain(smem_u32(st + Cfg::oSfA + 512), 0, 128));
+          const uint32_t tA = tbase + Cfg::kACol0 + s * 32;
+          const uint32_t ab = smem_u32(st + Cfg::oTok);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t idesc = idesc_mxf8f6f4(128, BN, kFmtE4M3, kFmtE2M3, kk, kk);
+            mma_mxf8f6f4_ts(tD, tA + kk * 8, sdesc_sw128(ab + kk * 32), idesc, tSfW, tSfA,
+                            (kt > sg.kt0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(smem_u32(&ctl.empty[s]));
+        }
+        tc_commit(smem_u32(&ctl.acc_full[buf]));
+        if (!ok) break;
+      }
+      // arrives once every tcgen05 operation this thread issued has completed
+      tc_commit(smem_u32(&ctl.drain));
+    }
+  } else if (warp >= 2 + Cfg::kEpiWarps) {
+    // ------------------------------------------------------------------ transcode
+    const int tw = warp - 2 - Cfg::kEpiWarps;   // 0..15
+    const int quarter = warp & 3;               // TMEM lane quarter this warp may access
+    const int j = tw >> 2;                      // K block (32 elements) of the stage
+    const int row = quarter * 32 + lane;
+    const bool tok_sf_warp = (tw == 0);
+    int i = 0;
+    Seg sg;
+    for (int idx = 0; sch.segment(cta, idx, sg) && !*abort_flag; ++idx) {
+      for (int kt = sg.kt0; kt < sg.kt1; ++kt, ++i) {
         const int s = i % S;
         const uint32_t ph = (i / S) & 1;
-        if (!mbar_wait(smem_u32(&ctl.ready[s]), ph, p.err, kErrWaitOperand, abort_flag)) break;
-        tc_fence_after();
+        if (!mbar_wait(smem_u32(&ctl.full[s]), ph, p.err, kErrWaitTma, abort_flag)) break;
         uint8_t* st = smem + s * Cfg::kStageBytes;
-        const uint32_t tSfW = tbase + Cfg::kSfCol0 + s * Cfg::kSfCols;
-        const uint32_t tSfA = tSfW + 4;
-        tmem_cp_32x128b_x4(tSfW, sdesc_plain(smem_u32(st + Cfg::oSfW), 0, 128));
-        tmem_cp_32x128b_x4(tSfA, sdesc_plain(smem_u32(st + Cfg::oSfA), 0, 128));
-        if constexpr (BN > 128)
-          tmem_cp_32x128b_x4(tSfA + 4, sdesc_plain(smem_u32(st + Cfg::oSfA + 512), 0, 128));
-        const uint32_t aw = smem_u32(st + Cfg::oW8), ab = smem_u32(st + Cfg::oA);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint32_t idesc = idesc_mxf8f6f4(128, BN, kFmtE4M3, kFmtE2M3, kk, kk);
-          mma_mxf8f6f4_ss(tD, sdesc_sw128(aw + kk * 32), sdesc_sw128(ab + kk * 32), idesc, tSfW,
-                          tSfA, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        tc_commit(smem_u32(&ctl.empty[s]));
-      }
-      tc_commit(smem_u32(&ctl.accum));
-    }
-  } else {
-    // ------------------------------------------------------------------ transcode
-    const int t = warp - 2;
-    for (int i = 0; i < nk; ++i) {
-      const int s = i % S;
-      const uint32_t ph = (i / S) & 1;
-      if (!mbar_wait(smem_u32(&ctl.full[s]), ph, p.err, kErrWaitTma, abort_flag)) break;
-      uint8_t* st = smem + s * Cfg::kStageBytes;
-#pragma unroll
-      for (int pass = 0; pass < 2; ++pass) {
-        const int row = pass * 64 + t * 8 + (lane >> 2);
-        const int blk = lane & 3;
-        const uint4 q = *reinterpret_cast<const uint4*>(st + Cfg::oWCode + row * 64 + blk * 16);
+        // 64B-swizzled codes: 16-byte chunk c of row r at r*64 + (c ^ ((r >> 1) & 3)) * 16
+        const uint4 q = *reinterpret_cast<const uint4*>(
+            st + Cfg::oWCode + row * 64 + ((j ^ ((row >> 1) & 3)) << 4));
         const uint32_t sc =
-            *reinterpret_cast<const uint16_t*>(st + Cfg::oWScale + row * 8 + blk * 2);
+            *reinterpret_cast<const uint16_t*>(st + Cfg::oWScale + row * 8 + j * 2);
         uint2 T0, T1;
         uint32_t e8;
         scale_pair(ctl.tab, sc & 0xFFu, sc >> 8, T0, T1, e8);
-        uint4 o0, o1;
-        transcode32<true>(q, T0, T1, o0, o1);
-        *reinterpret_cast<uint4*>(st + Cfg::oW8 + sw128_offset(row, blk * 2)) = o0;
-        *reinterpret_cast<uint4*>(st + Cfg::oW8 + sw128_offset(row, blk * 2 + 1)) = o1;
-        st[Cfg::oSfW + sf_offset(row, blk)] = static_cast<uint8_t>(e8);
-      }
-      if (t == 0) {
-        const uint32_t* raw = reinterpret_cast<const uint32_t*>(st + Cfg::oAScale);
-        uint32_t* pat = reinterpret_cast<uint32_t*>(st + Cfg::oSfA);
+        uint32_t v[8];
+        nib8_to_e4m3(q.x, T0, v[0], v[1]);
+        nib8_to_e4m3(q.y, T0, v[2], v[3]);
+        nib8_to_e4m3(q.z, T1, v[4], v[5]);
+        nib8_to_e4m3(q.w, T1, v[6], v[7]);
+        tmem_st_x8(tbase + Cfg::kACol0 + s * 32 + j * 8 + (static_cast<uint32_t>(quarter * 32) << 16),
+                   v);
+        st[Cfg::oSfW + sf_offset(row, j)] = static_cast<uint8_t>(e8);
+        if (tok_sf_warp) {
+          const uint32_t* raw = reinterpret_cast<const uint32_t*>(st + Cfg::oTokScale);
+          uint32_t* pat = reinterpret_cast<uint32_t*>(st + Cfg::oSfA);
 #pragma unroll
-        for (int n = lane; n < BN; n += 32)
-          pat[(n >> 7) * 128 + (n & 31) * 4 + ((n >> 5) & 3)] = raw[n];
+          for (int n = lane; n < BN; n += 32)
+            pat[(n >> 7) * 128 + (n & 31) * 4 + ((n >> 5) & 3)] = raw[n];
+        }
+        tmem_st_wait();
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&ctl.ready[s]));
       }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&ctl.ready[s]));
     }
-
-    // ------------------------------------------------------------------ epilogue
-    const bool ok = mbar_wait(smem_u32(&ctl.accum), 0, p.err, kErrWaitAccum, abort_flag);
-    tc_fence_after();
-    if (ok) {
-      const int q = warp & 3;
-      const int half = t >> 2;
-      const int n = n0 + q * 32 + lane;
-      constexpr int kHalf = BN / 2;
-      const uint32_t taddr = tbase + (static_cast<uint32_t>(q * 32) << 16);
-      for (int c0 = half * kHalf; c0 < (half + 1) * kHalf; c0 += 8) {
-        if (m0 + c0 >= p.M) break;  // uniform across the warp
-        uint32_t r[8];
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
-              "=r"(r[6]), "=r"(r[7])
-            : "r"(taddr + c0));
-        tmem_ld_wait();
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int quarter = warp & 3;
+    const int ep_tid = tid - 64;  // 0..127
+    Seg sg;
+    for (int idx = 0; sch.segment(cta, idx, sg); ++idx) {
+      const int buf = Cfg::kNumAcc == 2 ? (idx & 1) : 0;
+      const uint32_t use = Cfg::kNumAcc == 2 ? (idx >> 1) : idx;
+      if (!mbar_wait(smem_u32(&ctl.acc_full[buf]), use & 1, p.err, kErrWaitAccum, abort_flag))
+        break;
+      tc_fence_after();
+      const int mt = sg.tile / p.n_tiles, nt = sg.tile % p.n_tiles;
+      const int n = nt * 128 + quarter * 32 + lane;
+      const int m0 = mt * BN;
+      const int mcols = min(BN, p.M - m0);  // valid token columns of this tile
+      const uint32_t taddr =
+          tbase + buf * Cfg::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
+      const int row = quarter * 32 + lane;
+      bool finish = false;
+      if (sg.slot >= 0) {
+        // stream-K partial: store the slot, then count arrivals for this tile
+        float* slot = p.slots + (static_cast<int64_t>(cta) * 2 + sg.slot) * (BN * 128);
+        for (int c0 = 0; c0 < BN; c0 += 8) {
+          if (c0 >= mcols) break;
+          uint32_t r[8];
+          tmem_ld_x8(taddr + c0, r);
+          tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int m = m0 + c0 + j;
-          if (m < p.M) {
-            const float acc = __uint_as_float(r[j]);
-            if (p.out_mode == kOutC) {
-              const float v = apply_epilogue(acc * p.tensor_scale, p.epilogue, p.bias, n);
-              store_out(p.out, static_cast<int64_t>(m) * p.N + n, v, p.out_dtype);
-            } else if (p.out_mode == kOutPartial) {
-              reinterpret_cast<float*>(p.out)[(static_cast<int64_t>(split) * p.M + m) * p.N + n] =
-                  acc;
-            } else if (p.out_mode == kOutPlane) {
-              store_out(p.out, (static_cast<int64_t>(split) * p.M + m) * p.N + n,
-                        acc * p.tensor_scale, p.out_dtype);
-            } else {
-              atomicAdd(reinterpret_cast<float*>(p.out) + static_cast<int64_t>(m) * p.N + n,
-                        acc * p.tensor_scale);
+          for (int jj = 0; jj < 8; ++jj) __stcg(slot + (c0 + jj) * 128 + row, __uint_as_float(r[jj]));
+        }
+        __threadfence();
+        named_barrier(1, 32 * Cfg::kEpiWarps);
+        if (ep_tid == 0) {
+          const int first = sch.cta_of(static_cast<int64_t>(sg.tile) * p.nkt);
+          const int last = sch.cta_of(static_cast<int64_t>(sg.tile + 1) * p.nkt - 1);
+          const uint32_t old = atomicAdd(p.counters + sg.tile, 1u);
+          const bool fin = old == static_cast<uint32_t>(last - first);
+          if (fin) p.counters[sg.tile] = 0;  // every contributor has arrived: rearm
+          ctl.bcast = fin ? 1u : 0u;
+        }
+        named_barrier(1, 32 * Cfg::kEpiWarps);
+        finish = ctl.bcast != 0;
+        named_barrier(1, 32 * Cfg::kEpiWarps);
+      }
+      if (sg.slot < 0 || finish) {
+        const int first = sg.slot < 0 ? 0 : sch.cta_of(static_cast<int64_t>(sg.tile) * p.nkt);
+        const int last = sg.slot < 0 ? -1 : sch.cta_of(static_cast<int64_t>(sg.tile + 1) * p.nkt - 1);
+        if (finish) __threadfence();
+        for (int c0 = 0; c0 < BN; c0 += 8) {
+          if (c0 >= mcols) break;
+          float acc[8];
+          if (sg.slot < 0) {
+            uint32_t r[8];
+            tmem_ld_x8(taddr + c0, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) acc[jj] = __uint_as_float(r[jj]);
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) acc[jj] = 0.0f;
+            for (int c = first; c <= last; ++c) {
+              const int64_t cu0 = sch.u0(c);
+              const int sl = (cu0 / p.nkt == sg.tile) ? 0 : 1;
+              const float* slot = p.slots + (static_cast<int64_t>(c) * 2 + sl) * (BN * 128);
+#pragma unroll
+              for (int jj = 0; jj < 8; ++jj) acc[jj] += __ldcg(slot + (c0 + jj) * 128 + row);
+            }
+          }
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            const int m = m0 + c0 + jj;
+            if (c0 + jj < mcols) {
+              const float a = acc[jj];
+              if (p.split_k == 0 || p.split_k == 1) {
+                if (p.split_out == kOutAtomic) {
+                  atomicAdd(reinterpret_cast<float*>(p.out) + static_cast<int64_t>(m) * p.N + n,
+                            a * p.tensor_scale);
+                } else {
+                  store_out(p.out, static_cast<int64_t>(m) * p.N + n,
+                            apply_epilogue(a * p.tensor_scale, p.epilogue, p.bias, n),
+                            p.out_dtype);
+                }
+              } else if (p.split_out == kOutPartial) {
+                reinterpret_cast<float*>(p.out)[(static_cast<int64_t>(sg.z) * p.M + m) * p.N + n] = a;
+              } else if (p.split_out == kOutPlane) {
+                store_out(p.out, (static_cast<int64_t>(sg.z) * p.M + m) * p.N + n,
+                          a * p.tensor_scale, p.out_dtype);
+              } else {
+                atomicAdd(reinterpret_cast<float*>(p.out) + static_cast<int64_t>(m) * p.N + n,
+                          a * p.tensor_scale);
+              }
             }
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&ctl.acc_empty[buf]));
     }
   }
 
@@ -274,7 +458,8 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
-    if (lane == 0) mbar_wait(smem_u32(&ctl.accum), 0, p.err, kErrWaitAccum, nullptr);
+    // tensor memory is freed only after every MMA / copy the MMA thread issued is done
+    if (lane == 0) mbar_wait(smem_u32(&ctl.drain), 0, p.err, kErrWaitMma, nullptr);
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tbase, Cfg::kTmemCols);

@@ -114,23 +114,49 @@ def query_workspace(M: int, N: int, K: int, split_k: int = 0, split_mode: str = 
     return int(_lib.load().bd_query_workspace(M, N, K, split_k, SPLIT_MODES[split_mode]))
 
 
-def choose_split_k(M: int, N: int, K: int) -> int:
-    s = int(_lib.load().bd_choose_split_k(M, N, K))
-    _lib.check("bd_choose_split_k", min(s, 0))
-    return s
+class Workspace:
+    """Device scratch for bd_w4a6_gemm. Zeroed when allocated and whenever the problem shape
+    changes; between calls of one shape the stream-K counters are left at zero by the kernel
+    itself, so repeated calls (and CUDA-graph replays) need no clearing. One per stream."""
+
+    def __init__(self, device=None):
+        self.buf = None
+        self.device = device
+        self.key = None
+
+    def get(self, nbytes: int, device, key=None) -> Optional[torch.Tensor]:
+        if nbytes == 0:
+            return None
+        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != device:
+            self.buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        elif key != self.key:
+            self.buf[:nbytes].zero_()
+        self.key = key
+        return self.buf
+
+
+_default_ws = {}
+
+
+def _workspace_for(device, stream) -> Workspace:
+    key = (str(device), int(_stream(stream).value or 0))
+    if key not in _default_ws:
+        _default_ws[key] = Workspace()
+    return _default_ws[key]
 
 
 def w4a6_gemm(acts: PackedActivations, weights: PackedWeights,
               bias: Optional[torch.Tensor] = None, out_dtype=torch.bfloat16,
               epilogue: str = "none", split_k: int = 0, split_mode: str = "reduce",
-              out: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
+              out: Optional[torch.Tensor] = None, workspace=None,
               stream=None) -> torch.Tensor:
-    """C[M, N] = A . B^T * tensor_scale (+ bias, activation) on the tensor cores."""
+    """C[M, N] = A . B^T * tensor_scale (+ bias, activation) on the tensor cores.
+
+    split_k=0 (default) runs the persistent stream-K schedule; its scratch comes from
+    `workspace` (a zeroed uint8 tensor or a Workspace), else from a per-stream Workspace."""
     M, K, N = acts.M, acts.K, weights.N
     if weights.K != K:
         raise ValueError(f"K mismatch: activations {K}, weights {weights.K}")
-    if split_k == 0:
-        split_k = choose_split_k(M, N, K)
     planes = split_k if (split_mode == "planes" and split_k > 1) else 1
     if out is None:
         shape = (planes, M, N) if planes > 1 else (M, N)
@@ -138,8 +164,12 @@ def w4a6_gemm(acts: PackedActivations, weights: PackedWeights,
         out = alloc(shape, dtype=out_dtype, device=acts.codes.device)
     _need(out, out_dtype, "out", planes * M * N)
     ws_bytes = query_workspace(M, N, K, split_k, split_mode)
-    if ws_bytes and workspace is None:
-        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=acts.codes.device)
+    key = (M, N, K, split_k, split_mode)
+    if isinstance(workspace, Workspace):
+        workspace = workspace.get(ws_bytes, acts.codes.device, key)
+    elif workspace is None and ws_bytes:
+        workspace = _workspace_for(acts.codes.device, stream).get(ws_bytes, acts.codes.device,
+                                                                  key)
     if bias is not None:
         _need(bias, torch.bfloat16, "bias", N)
     epi = EPILOGUES[epilogue]

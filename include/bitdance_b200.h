@@ -103,17 +103,23 @@ int bd_pack_b(const uint8_t* codes, const uint8_t* scales16, uint8_t* codes_tile
 int bd_pack_a(const uint8_t* codes, const uint8_t* e8m0, uint8_t* a_packed,
               uint8_t* scales_tiled, int M, int K, bd_stream_t stream);
 
-/* Bytes of workspace bd_w4a6_gemm needs for this problem (0 when split_k resolves to 1 or the
- * split mode needs none). split_k == 0 means "let the library choose". */
+/* Bytes of workspace bd_w4a6_gemm needs on the current device for this problem.
+ * split_k == 0 (stream-K, the default schedule): per-CTA fp32 partial slots plus one arrival
+ * counter per output tile. The workspace must be ZEROED before its first use with a given
+ * (M, N, K); every call leaves it ready for the next call of the same shape (its counters back
+ * at zero). Zero it again before reusing it for another shape (the layout of slots and
+ * counters depends on the shape). Calls that run concurrently on the GPU must not share one
+ * workspace.
+ * split_k > 1 with BD_SPLIT_REDUCE: split_k fp32 planes of M x N. Otherwise 0. */
 size_t bd_query_workspace(int M, int N, int K, int split_k, int split_mode);
-
-/* The split_k the library would use for split_k == 0 (auto). */
-int bd_choose_split_k(int M, int N, int K);
 
 /* C[M,N] = (A . B^T) * b_tensor_scale (+ bias[N], activation), fp32 accumulation.
  * A: MXFP6 (bd_pack_a layout); B: NVFP4 (bd_pack_b tiled layout), transcoded on chip to MXFP6
  * per the reference contract and fed to block-scaled tcgen05 MMAs.
- * Shapes: M >= 1, N % 128 == 0, K % 128 == 0, (K/128) % split_k == 0.
+ * Shapes: M >= 1, N % 128 == 0, K % 128 == 0, (K/128) % split_k == 0 when split_k > 0.
+ * split_k == 0: persistent stream-K schedule over (tile, 128-wide K chunk) units, tiles split
+ * between CTAs finished in-kernel in a fixed order (needs the workspace, see above).
+ * split_k >= 1: each tile's K range cut into split_k pieces; split_mode says how they combine.
  * bias: N bf16 values (used when epilogue != BD_EPI_NONE). With split_mode PLANES, c holds
  * split_k planes; with ATOMIC, out_dtype must be BD_OUT_F32 and epilogue BD_EPI_NONE.
  * Replaces compile_preshuffle_gemm_a8(in_dtype="w4a6_tc") + launch_fn

@@ -153,17 +153,15 @@ int orc_transcode(const uint8_t* codes_packed, const uint8_t* scales, int64_t nb
   return 0;
 }
 
-typedef struct { const uint8_t* e2m3; const uint8_t* e8m0; float* out; float mag[32]; } dequant_ctx;
+typedef struct { const uint8_t* e2m3; const uint8_t* e8m0; float* out; float val[64]; } dequant_ctx;
 
 static void dequant_range(const void* p, int64_t lo, int64_t hi) {
   const dequant_ctx* c = (const dequant_ctx*)p;
   for (int64_t b = lo; b < hi; ++b) {
-    float s = ldexpf(1.0f, (int)c->e8m0[b] - 127);
-    for (int i = 0; i < 32; ++i) {
-      uint8_t v = c->e2m3[b * 32 + i];
-      float x = c->mag[v & 31] * s;
-      c->out[b * 32 + i] = (v & 32) ? -x : x;
-    }
+    const float s = ldexpf(1.0f, (int)c->e8m0[b] - 127);
+    const uint8_t* in = c->e2m3 + b * 32;
+    float* out = c->out + b * 32;
+    for (int i = 0; i < 32; ++i) out[i] = c->val[in[i] & 63] * s;
   }
 }
 
@@ -173,7 +171,7 @@ int orc_dequant(const uint8_t* e2m3, const uint8_t* e8m0, int64_t nblk32, float*
   if (nblk32 < 0) return -1;
   dequant_ctx c;
   c.e2m3 = e2m3; c.e8m0 = e8m0; c.out = out;
-  for (int i = 0; i < 32; ++i) c.mag[i] = (float)e2m3_mag(i);
+  for (int i = 0; i < 64; ++i) c.val[i] = (i & 32 ? -1.0f : 1.0f) * (float)e2m3_mag(i & 31);
   parallel_for(nblk32, nthreads, dequant_range, &c);
   return 0;
 }

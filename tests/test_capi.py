@@ -90,13 +90,11 @@ def test_workspace_query(lib):
     assert lib.bd_query_workspace(64, 1024, 1024, 4, 1) == 0   # planes need none
     assert lib.bd_query_workspace(64, 1024, 1024, 1, 0) == 0
     assert lib.bd_query_workspace(64, 1000, 1024, 4, 0) == 0   # invalid shape
-
-
-def test_split_choice_fills_the_machine(lib):
-    # 112 weight tiles on 148 SMs: the library splits K
-    s = lib.bd_choose_split_k(16, 14336, 4096)
-    assert s >= 2 and (4096 // 128) % s == 0
-    assert lib.bd_choose_split_k(8192, 14336, 4096) == 1
+    # stream-K (split_k 0): slots for (grid x 2) partial tiles + one counter per tile; with no
+    # device visible the library assumes 148 SMs
+    tiles = 14336 // 128
+    slots = 148 * 2 * 16 * 128 * 4
+    assert lib.bd_query_workspace(16, 14336, 4096, 0, 0) == slots + (tiles * 4 + 255) // 256 * 256
 
 
 def test_psg_shim_validation_matches_reference_errors():

@@ -182,5 +182,59 @@ def test_rejects_unsupported_shapes_and_small_workspace():
         bd.w4a6_gemm(acts, w, split_k=4, split_mode="reduce", workspace=ws)
     assert e.value.status == _lib.BD_ERR_WORKSPACE
     with pytest.raises(BitdanceError) as e:
+        bd.w4a6_gemm(acts, w, split_k=0, workspace=ws)
+    assert e.value.status == _lib.BD_ERR_WORKSPACE
+    with pytest.raises(BitdanceError) as e:
         bd.w4a6_gemm(acts, w, split_k=3)
     assert e.value.status == _lib.BD_ERR_SHAPE
+
+
+@pytest.mark.parametrize("M,N,K", [(16, 2048, 4096), (64, 256, 4096), (1, 128, 128),
+                                   (300, 384, 1024), (16, 14336, 1024), (5, 1024, 8192),
+                                   (129, 640, 2048)])
+def test_streamk_schedule(M, N, K):
+    """Default schedule: tiles split between CTAs (up to 32 contributors per tile), fixed up
+    in-kernel; repeated calls reuse the workspace and give bit-identical results."""
+    import bitdance_b200 as bd
+    ops = random_operands(M, N, K, seed=M + N + K)
+    C, Cabs = gold(*ops, 0.75)
+    acts = bd.pack_activations(dev(ops[0]), dev(ops[1]))
+    w = bd.pack_weights(dev(ops[2]), dev(ops[3]), 0.75)
+    ws = bd.Workspace()
+    first = bd.w4a6_gemm(acts, w, workspace=ws)
+    second = bd.w4a6_gemm(acts, w, workspace=ws)
+    torch.cuda.synchronize()
+    assert bd.device_error() == 0
+    check(first, C, Cabs)
+    assert torch.equal(first, second)
+    # the arrival counters (the tail of the workspace) are back at zero after every call
+    nbytes = bd.query_workspace(M, N, K, 0)
+    bn = 16 if M <= 16 else 32 if M <= 32 else 64 if M <= 64 else 128 if M <= 128 else 256
+    tiles = (N // 128) * ((M + bn - 1) // bn)
+    counter_bytes = (tiles * 4 + 255) // 256 * 256
+    assert int(ws.buf[nbytes - counter_bytes:nbytes].count_nonzero()) == 0
+
+
+def test_streamk_epilogues_and_dtypes():
+    M, N, K = 24, 512, 2048
+    ops = random_operands(M, N, K, seed=77, b_scale_lo=0x18, b_scale_hi=0x30)
+    bias = (np.random.default_rng(6).standard_normal(N) * 4).astype(np.float32)
+    bias_bf = torch.from_numpy(bias).to(torch.bfloat16)
+    C, Cabs = gold(*ops, 0.05, bias_bf.float().numpy().astype(np.float64))
+    C = C * 0.5 * (1 + np.tanh(0.5 * C))   # SiLU without overflow
+    got = run_gpu(*ops, 0.05, bias=bias_bf.cuda(), epilogue="bias_silu", out_dtype=torch.float16)
+    g = got.float().cpu().numpy()
+    assert o.rel_linf(C, g) <= TOL_REL_LINF
+
+
+def test_workspace_reused_across_shapes():
+    """One Workspace serving several problem shapes in turn (it re-zeroes on a shape change)."""
+    import bitdance_b200 as bd
+    ws = bd.Workspace()
+    for i, (M, N, K) in enumerate([(128, 4096, 1024), (1, 2048, 4096), (16, 2048, 4096),
+                                   (128, 4096, 1024), (16, 2048, 4096)]):
+        ops = random_operands(M, N, K, seed=100 + i)
+        C, Cabs = gold(*ops, 1.0)
+        acts = bd.pack_activations(dev(ops[0]), dev(ops[1]))
+        w = bd.pack_weights(dev(ops[2]), dev(ops[3]), 1.0)
+        check(bd.w4a6_gemm(acts, w, workspace=ws), C, Cabs)
