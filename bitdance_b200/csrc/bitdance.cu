@@ -90,6 +90,19 @@ bool make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, void* base, uint64_t d0
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool make_map_3d(CUtensorMap* m, CUtensorMapDataType dt, void* base, uint64_t d0, uint64_t d1,
+                 uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0,
+                 uint32_t b1, uint32_t b2, CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  const cuuint32_t box[3] = {b0, b1, b2};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, dt, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int grid_for(int64_t work, int per_block, const DeviceInfo* d) {
   int64_t blocks = (work + per_block - 1) / per_block;
   const int64_t cap = static_cast<int64_t>(d->sm_count) * 8;
@@ -123,22 +136,46 @@ StreamKSizes streamk_sizes(int M, int N, int K, int sm_count) {
   return z;
 }
 
-template <int BN>
-int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tas, const CUtensorMap& tw,
-                   const GemmParams& p, int grid, cudaStream_t stream) {
-  using Cfg = GemmCfg<BN>;
+struct GemmMaps {
+  CUtensorMap a, as, w, ws;
+};
+
+template <int BN, int KS>
+int launch_gemm(const GemmMaps& m, const GemmParams& p, int grid, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN, KS>;
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load() & bit)) {
-    if (cudaFuncSetAttribute(w4a6_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(w4a6_gemm_kernel<BN, KS>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Cfg::kSmemBytes) != cudaSuccess)
       return BD_ERR_CUDA;
     configured.fetch_or(bit);
   }
-  w4a6_gemm_kernel<BN><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tas, tw, p);
+  w4a6_gemm_kernel<BN, KS><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(m.a, m.as, m.w,
+                                                                              m.ws, p);
   return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
+}
+
+int launch_gemm_any(int bn, int ks, const GemmMaps& m, const GemmParams& p, int grid,
+                    cudaStream_t s) {
+  if (ks == 2) {
+    switch (bn) {
+      case 16: return launch_gemm<16, 2>(m, p, grid, s);
+      case 32: return launch_gemm<32, 2>(m, p, grid, s);
+      case 64: return launch_gemm<64, 2>(m, p, grid, s);
+      default: return launch_gemm<128, 2>(m, p, grid, s);
+    }
+  }
+  switch (bn) {
+    case 16: return launch_gemm<16, 1>(m, p, grid, s);
+    case 32: return launch_gemm<32, 1>(m, p, grid, s);
+    case 64: return launch_gemm<64, 1>(m, p, grid, s);
+    case 128: return launch_gemm<128, 1>(m, p, grid, s);
+    default: return launch_gemm<256, 1>(m, p, grid, s);
+  }
 }
 
 }  // namespace
@@ -310,20 +347,25 @@ int bd_w4a6_gemm(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8
     if (!aligned(workspace, 16) || N % 4) return BD_ERR_ALIGNMENT;
   }
 
+  // pipeline stages of two 128-wide K chunks when the shape allows it
+  const int ks = (bn <= 128 && nkt % 2 == 0 && (split_k == 0 || (nkt / 2) % split_k == 0)) ? 2 : 1;
+  const int nks = nkt / ks;
   const int Mp4 = (M + 3) / 4 * 4;
-  CUtensorMap ta, tas, tw;
-  if (!make_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, const_cast<uint8_t*>(a), K, M, K, 128, bn,
-                   CU_TENSOR_MAP_SWIZZLE_128B))
+  GemmMaps maps;
+  if (!make_map_3d(&maps.a, CU_TENSOR_MAP_DATA_TYPE_UINT8, const_cast<uint8_t*>(a), 128, M, nkt,
+                   K, 128, 128, bn, ks, CU_TENSOR_MAP_SWIZZLE_128B))
     return BD_ERR_CUDA;
-  if (!make_map_2d(&tas, CU_TENSOR_MAP_DATA_TYPE_UINT32, const_cast<uint8_t*>(a_scales), Mp4,
-                   nkt, static_cast<uint64_t>(Mp4) * 4, bn, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
+  if (!make_map_2d(&maps.as, CU_TENSOR_MAP_DATA_TYPE_UINT32, const_cast<uint8_t*>(a_scales), Mp4,
+                   nkt, static_cast<uint64_t>(Mp4) * 4, bn, ks, CU_TENSOR_MAP_SWIZZLE_NONE))
     return BD_ERR_CUDA;
-  if (!make_map_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, const_cast<uint8_t*>(b), 64,
-                   static_cast<uint64_t>(N) * nkt, 64, 64, 128, CU_TENSOR_MAP_SWIZZLE_64B))
+  if (!make_map_2d(&maps.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, const_cast<uint8_t*>(b), 64,
+                   static_cast<uint64_t>(N) * nkt, 64, 64, 128 * ks, CU_TENSOR_MAP_SWIZZLE_64B))
+    return BD_ERR_CUDA;
+  if (!make_map_2d(&maps.ws, CU_TENSOR_MAP_DATA_TYPE_UINT32, const_cast<uint8_t*>(b_scales), 256,
+                   static_cast<uint64_t>(n_tiles) * nkt, 1024, 256, ks, CU_TENSOR_MAP_SWIZZLE_NONE))
     return BD_ERR_CUDA;
 
   GemmParams p;
-  p.wscales = b_scales;
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.tensor_scale = b_tensor_scale;
   p.M = M;
@@ -331,7 +373,7 @@ int bd_w4a6_gemm(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8
   p.K = K;
   p.n_tiles = n_tiles;
   p.m_tiles = m_tiles;
-  p.nkt = nkt;
+  p.nks = nks;
   p.split_k = streamk ? 0 : split_k;
   p.out_dtype = out_dtype;
   p.epilogue = epilogue;
@@ -345,21 +387,13 @@ int bd_w4a6_gemm(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8
     p.split_out = kOutPartial;
     p.out = workspace;
   } else p.split_out = kOutPlane;
-  int64_t work = streamk ? tiles * nkt : tiles * split_k;
+  const int64_t work = streamk ? tiles * nks : tiles * split_k;
   if (streamk) {
     p.slots = static_cast<float*>(workspace);
     p.counters = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + sk.slots_bytes);
   }
   const int grid = static_cast<int>(work < d->sm_count ? work : d->sm_count);
-  cudaStream_t s = as_stream(stream);
-  int rc;
-  switch (bn) {
-    case 16: rc = launch_gemm_bn<16>(ta, tas, tw, p, grid, s); break;
-    case 32: rc = launch_gemm_bn<32>(ta, tas, tw, p, grid, s); break;
-    case 64: rc = launch_gemm_bn<64>(ta, tas, tw, p, grid, s); break;
-    case 128: rc = launch_gemm_bn<128>(ta, tas, tw, p, grid, s); break;
-    default: rc = launch_gemm_bn<256>(ta, tas, tw, p, grid, s); break;
-  }
+  const int rc = launch_gemm_any(bn, ks, maps, p, grid, as_stream(stream));
   if (rc != BD_OK || !use_ws) return rc;
   return bd_splitk_reduce(static_cast<const float*>(workspace), c, bias, b_tensor_scale, M, N,
                           split_k, out_dtype, epilogue, stream);

@@ -44,30 +44,32 @@ constexpr int cpow2(int x) {
   return p;
 }
 
-template <int BN>
+template <int BN, int KS>
 struct GemmCfg {
-  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 5 : 8);
-  static constexpr int kTok = BN * 128;       // token tile (E2M3 operand image), SW128
-  static constexpr int kWCode = 128 * 64;     // packed NVFP4 codes, SW64
-  static constexpr int kWScale = 128 * 8;     // E4M3 per-16 scales
-  static constexpr int kTokScale = cround(BN * 4, 128);
-  static constexpr int kSfA = BN > 128 ? 1024 : 512;
+  // KS 128-wide K chunks per pipeline stage
+  static constexpr int kStages = KS == 2 ? (BN >= 128 ? 3 : (BN >= 64 ? 4 : 5))
+                                         : (BN >= 256 ? 4 : (BN >= 128 ? 5 : 8));
+  static constexpr int kTok = KS * BN * 128;     // token tiles (E2M3 operand image), SW128
+  static constexpr int kWCode = KS * 128 * 64;   // packed NVFP4 codes, SW64
+  static constexpr int kWScale = KS * 128 * 8;   // E4M3 per-16 scales
+  static constexpr int kTokScale = cround(KS * BN * 4, 128);
   static constexpr int oTok = 0;
   static constexpr int oWCode = cround(oTok + kTok, 1024);
   static constexpr int oWScale = oWCode + kWCode;
   static constexpr int oTokScale = oWScale + kWScale;
-  static constexpr int oSfW = oTokScale + kTokScale;
-  static constexpr int oSfA = oSfW + 512;
-  static constexpr int kStageBytes = cround(oSfA + kSfA, 1024);
-  static constexpr int kTxBytes = kWCode + kWScale + kTok + BN * 4;
-  // tensor memory: accumulators, then per stage 32 columns of A (128 B of K per lane) and
-  // the scale factors (4 columns for the weights, 4 or 8 for the tokens)
-  static constexpr int kSfCols = 4 + (BN > 128 ? 8 : 4);
+  static constexpr int kStageBytes = cround(oTokScale + kTokScale, 1024);
+  static constexpr int kTxBytes = kWCode + kWScale + kTok + KS * BN * 4;
+  // tensor memory: accumulators | A operand (32 columns per chunk) | scale factors: per chunk
+  // 4 columns of weight scales (quarter q uses column q) + BN/32 columns of token scales,
+  // padded so every scale-factor address the MMA gets is a multiple of 4 columns
+  static constexpr int kTokSfCols = BN >= 32 ? BN / 32 : 1;
+  static constexpr int kSfColsPerChunk = 4 + cround(kTokSfCols, 4);
   static constexpr int kAccCols = BN < 32 ? 32 : BN;
-  static constexpr int kNumAcc = (2 * kAccCols + kStages * (32 + kSfCols) <= 512) ? 2 : 1;
+  static constexpr int kPerStageCols = KS * (32 + kSfColsPerChunk);
+  static constexpr int kNumAcc = (2 * kAccCols + kStages * kPerStageCols <= 512) ? 2 : 1;
   static constexpr int kACol0 = kNumAcc * kAccCols;
-  static constexpr int kSfCol0 = kACol0 + kStages * 32;
-  static constexpr int kTmemCols = cpow2(kSfCol0 + kStages * kSfCols);
+  static constexpr int kSfCol0 = kACol0 + kStages * KS * 32;
+  static constexpr int kTmemCols = cpow2(kSfCol0 + kStages * KS * kSfColsPerChunk);
   static constexpr int oCtl = kStages * kStageBytes;
   static constexpr int kCtlBytes = 2048;
   static constexpr int kSmemBytes = oCtl + kCtlBytes + 1024;  // + alignment slack
@@ -77,6 +79,8 @@ struct GemmCfg {
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static_assert(kTmemCols <= 512, "tensor memory budget");
   static_assert(kStages <= 8, "control block holds 8 stages");
+  static_assert(kSfCol0 % 4 == 0 && kSfColsPerChunk % 4 == 0 && kACol0 % 8 == 0,
+                "tensor-memory operand addresses stay 4-column aligned");
 };
 
 struct GemmCtl {
@@ -88,37 +92,36 @@ struct GemmCtl {
 };
 
 struct GemmParams {
-  const uint8_t* wscales;       // [N/128][K/128][128][8] (codes come through the tensor map)
   void* out;                    // C, or the fp32 workspace planes (kOutPartial)
   float* slots;                 // stream-K partial slots [grid][2][BN][128]
   uint32_t* counters;           // stream-K per-tile arrival counters (zero between calls)
   const __nv_bfloat16* bias;
   float tensor_scale;
   int M, N, K;
-  int n_tiles, m_tiles, nkt;
+  int n_tiles, m_tiles, nks;    // nks: pipeline stages (KS chunks) per tile
   int split_k;                  // 0 = stream-K, else explicit split
   int split_out;                // output mode of explicit split segments
   int out_dtype, epilogue;
   uint32_t* err;
 };
 
-// One contiguous run of K chunks of one tile.
+// One contiguous run of stages of one tile.
 struct Seg {
-  int tile, kt0, kt1, z, slot;  // slot: -1 full tile, 0/1 stream-K partial slot
+  int tile, k0, k1, z, slot;  // slot: -1 full tile, 0/1 stream-K partial slot
 };
 
 // The work of CTA `c` of `G`: segment number `idx` (false when there is none).
 struct Schedule {
-  int64_t U;    // units (tile, K chunk)
+  int64_t U;    // units (tile, stage)
   int64_t q, r; // stream-K: U = q*G + r
-  int G, nkt, tiles, split;
+  int G, nks, tiles, split;
 
   __device__ __forceinline__ void init(const GemmParams& p, int grid) {
     G = grid;
-    nkt = p.nkt;
+    nks = p.nks;
     tiles = p.n_tiles * p.m_tiles;
     split = p.split_k;
-    U = static_cast<int64_t>(tiles) * nkt;
+    U = static_cast<int64_t>(tiles) * nks;
     q = U / G;
     r = U % G;
   }
@@ -135,23 +138,23 @@ struct Schedule {
       if (item >= static_cast<int64_t>(tiles) * split) return false;
       s.tile = static_cast<int>(item / split);
       s.z = static_cast<int>(item % split);
-      const int per = nkt / split;
-      s.kt0 = s.z * per;
-      s.kt1 = s.kt0 + per;
+      const int per = nks / split;
+      s.k0 = s.z * per;
+      s.k1 = s.k0 + per;
       s.slot = -1;
       return true;
     }
     const int64_t a = u0(c), b = u0(c + 1);
     if (a >= b) return false;
-    const int64_t t = a / nkt + idx;
-    const int64_t lo = a > t * nkt ? a : t * nkt;
-    const int64_t hi = b < (t + 1) * nkt ? b : (t + 1) * nkt;
+    const int64_t t = a / nks + idx;
+    const int64_t lo = a > t * nks ? a : t * nks;
+    const int64_t hi = b < (t + 1) * nks ? b : (t + 1) * nks;
     if (lo >= hi) return false;
     s.tile = static_cast<int>(t);
-    s.kt0 = static_cast<int>(lo - t * nkt);
-    s.kt1 = static_cast<int>(hi - t * nkt);
+    s.k0 = static_cast<int>(lo - t * nks);
+    s.k1 = static_cast<int>(hi - t * nks);
     s.z = 0;
-    s.slot = (s.kt0 == 0 && s.kt1 == nkt) ? -1 : (idx == 0 ? 0 : 1);
+    s.slot = (s.k0 == 0 && s.k1 == nks) ? -1 : (idx == 0 ? 0 : 1);
     return true;
   }
 };
@@ -195,12 +198,20 @@ __device__ __forceinline__ void nib8_to_e4m3(uint32_t w, uint2 T, uint32_t& lo, 
   hi = (prmt(t, w, 0x7362u) & 0x80808080u) | prmt(T.x, T.y, m >> 16);
 }
 
-template <int BN>
-__global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
+// E8M0 byte of a 32-block from its two E4M3 scale bytes.
+__device__ __forceinline__ uint32_t e8m0_of_pair(const TranscodeTables& t, uint32_t s0,
+                                                 uint32_t s1) {
+  const int e0 = t.info[s0 & 0x7Fu] >> 3, e1 = t.info[s1 & 0x7Fu] >> 3;
+  return static_cast<uint32_t>(max(e0, e1) + 111);
+}
+
+template <int BN, int KS>
+__global__ void __launch_bounds__(GemmCfg<BN, KS>::kThreads, 1)
     w4a6_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
                      const __grid_constant__ CUtensorMap tm_as,
-                     const __grid_constant__ CUtensorMap tm_w, const GemmParams p) {
-  using Cfg = GemmCfg<BN>;
+                     const __grid_constant__ CUtensorMap tm_w,
+                     const __grid_constant__ CUtensorMap tm_ws, const GemmParams p) {
+  using Cfg = GemmCfg<BN, KS>;
   constexpr int S = Cfg::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -230,6 +241,7 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
     prefetch_tmap(&tm_a);
     prefetch_tmap(&tm_as);
     prefetch_tmap(&tm_w);
+    prefetch_tmap(&tm_ws);
   }
   load_tables<true>(ctl.tab, tid, Cfg::kThreads);
   if (warp == 1) {
@@ -248,17 +260,18 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
       Seg sg;
       for (int idx = 0; sch.segment(cta, idx, sg) && !*abort_flag; ++idx) {
         const int mt = sg.tile / p.n_tiles, nt = sg.tile % p.n_tiles;
-        for (int kt = sg.kt0; kt < sg.kt1; ++kt, ++i) {
+        for (int k = sg.k0; k < sg.k1; ++k, ++i) {
           const int s = i % S;
           const uint32_t ph = (i / S) & 1;
           if (!mbar_wait(smem_u32(&ctl.empty[s]), ph ^ 1u, p.err, kErrWaitEmpty, abort_flag)) break;
           uint8_t* st = smem + s * Cfg::kStageBytes;
           const uint32_t fb = smem_u32(&ctl.full[s]);
-          const int64_t chunk = static_cast<int64_t>(nt) * p.nkt + kt;
+          const int kt = k * KS;
+          const int32_t chunk = nt * (p.nks * KS) + kt;
           mbar_arrive_expect_tx(fb, Cfg::kTxBytes);
-          tma_load_2d(smem_u32(st + Cfg::oWCode), &tm_w, 0, static_cast<int32_t>(chunk * 128), fb);
-          bulk_load(smem_u32(st + Cfg::oWScale), p.wscales + chunk * 1024, 1024, fb);
-          tma_load_2d(smem_u32(st + Cfg::oTok), &tm_a, kt * 128, mt * BN, fb);
+          tma_load_2d(smem_u32(st + Cfg::oWCode), &tm_w, 0, chunk * 128, fb);
+          tma_load_2d(smem_u32(st + Cfg::oWScale), &tm_ws, 0, chunk, fb);
+          tma_load_3d(smem_u32(st + Cfg::oTok), &tm_a, 0, mt * BN, kt, fb);
           tma_load_2d(smem_u32(st + Cfg::oTokScale), &tm_as, mt * BN, kt, fb);
         }
       }
@@ -277,7 +290,7 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
         tc_fence_after();
         const uint32_t tD = tbase + buf * Cfg::kAccCols;
         bool ok = true;
-        for (int kt = sg.kt0; kt < sg.kt1; ++kt, ++i) {
+        for (int k = sg.k0; k < sg.k1; ++k, ++i) {
           const int s = i % S;
           const uint32_t ph = (i / S) & 1;
           if (!mbar_wait(smem_u32(&ctl.ready[s]), ph, p.err, kErrWaitOperand, abort_flag)) {
@@ -285,20 +298,19 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
             break;
           }
           tc_fence_after();
-          uint8_t* st = smem + s * Cfg::kStageBytes;
-          const uint32_t tSfW = tbase + Cfg::kSfCol0 + s * Cfg::kSfCols;
-          const uint32_t tSfA = tSfW + 4;
-          tmem_cp_32x128b_x4(tSfW, sdesc_plain(smem_u32(st + Cfg::oSfW), 0, 128));
-          tmem_cp_32x128b_x4(tSfA, sdesc_plain(smem_u32(st + Cfg::oSfA), 0, 128));
-          if constexpr (BN > 128)
-            tmem_cp_32x128b_x4(tSfA + 4, sdesc_plain(smem_u32(st + Cfg::oSfA + 512), 0, 128));
-          const uint32_t tA = tbase + Cfg::kACol0 + s * 32;
-          const uint32_t ab = smem_u32(st + Cfg::oTok);
+          const uint32_t tok = smem_u32(smem + s * Cfg::kStageBytes + Cfg::oTok);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t idesc = idesc_mxf8f6f4(128, BN, kFmtE4M3, kFmtE2M3, kk, kk);
-            mma_mxf8f6f4_ts(tD, tA + kk * 8, sdesc_sw128(ab + kk * 32), idesc, tSfW, tSfA,
-                            (kt > sg.kt0 || kk > 0) ? 1u : 0u);
+          for (int h = 0; h < KS; ++h) {
+            const uint32_t tA = tbase + Cfg::kACol0 + (s * KS + h) * 32;
+            const uint32_t tSfW = tbase + Cfg::kSfCol0 + (s * KS + h) * Cfg::kSfColsPerChunk;
+            const uint32_t tSfA = tSfW + 4;
+            const uint32_t ab = tok + h * BN * 128;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint32_t idesc = idesc_mxf8f6f4(128, BN, kFmtE4M3, kFmtE2M3, kk, kk);
+              mma_mxf8f6f4_ts(tD, tA + kk * 8, sdesc_sw128(ab + kk * 32), idesc, tSfW, tSfA,
+                              (k > sg.k0 || h > 0 || kk > 0) ? 1u : 0u);
+            }
           }
           tc_commit(smem_u32(&ctl.empty[s]));
         }
@@ -312,42 +324,61 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
     // ------------------------------------------------------------------ transcode
     const int tw = warp - 2 - Cfg::kEpiWarps;   // 0..15
     const int quarter = warp & 3;               // TMEM lane quarter this warp may access
-    const int j = tw >> 2;                      // K block (32 elements) of the stage
+    const int j = tw >> 2;                      // K block (32 elements) of each chunk
     const int row = quarter * 32 + lane;
-    const bool tok_sf_warp = (tw == 0);
+    const uint32_t lane_base = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
     int i = 0;
     Seg sg;
     for (int idx = 0; sch.segment(cta, idx, sg) && !*abort_flag; ++idx) {
-      for (int kt = sg.kt0; kt < sg.kt1; ++kt, ++i) {
+      for (int k = sg.k0; k < sg.k1; ++k, ++i) {
         const int s = i % S;
         const uint32_t ph = (i / S) & 1;
         if (!mbar_wait(smem_u32(&ctl.full[s]), ph, p.err, kErrWaitTma, abort_flag)) break;
-        uint8_t* st = smem + s * Cfg::kStageBytes;
-        // 64B-swizzled codes: 16-byte chunk c of row r at r*64 + (c ^ ((r >> 1) & 3)) * 16
-        const uint4 q = *reinterpret_cast<const uint4*>(
-            st + Cfg::oWCode + row * 64 + ((j ^ ((row >> 1) & 3)) << 4));
-        const uint32_t sc =
-            *reinterpret_cast<const uint16_t*>(st + Cfg::oWScale + row * 8 + j * 2);
-        uint2 T0, T1;
-        uint32_t e8;
-        scale_pair(ctl.tab, sc & 0xFFu, sc >> 8, T0, T1, e8);
-        uint32_t v[8];
-        nib8_to_e4m3(q.x, T0, v[0], v[1]);
-        nib8_to_e4m3(q.y, T0, v[2], v[3]);
-        nib8_to_e4m3(q.z, T1, v[4], v[5]);
-        nib8_to_e4m3(q.w, T1, v[6], v[7]);
-        tmem_st_x8(tbase + Cfg::kACol0 + s * 32 + j * 8 + (static_cast<uint32_t>(quarter * 32) << 16),
-                   v);
-        st[Cfg::oSfW + sf_offset(row, j)] = static_cast<uint8_t>(e8);
-        if (tok_sf_warp) {
-          const uint32_t* raw = reinterpret_cast<const uint32_t*>(st + Cfg::oTokScale);
-          uint32_t* pat = reinterpret_cast<uint32_t*>(st + Cfg::oSfA);
+        const uint8_t* st = smem + s * Cfg::kStageBytes;
 #pragma unroll
-          for (int n = lane; n < BN; n += 32)
-            pat[(n >> 7) * 128 + (n & 31) * 4 + ((n >> 5) & 3)] = raw[n];
+        for (int h = 0; h < KS; ++h) {
+          // 64B-swizzled codes: 16-byte chunk c of row r at r*64 + (c ^ ((r >> 1) & 3)) * 16
+          const uint4 q = *reinterpret_cast<const uint4*>(
+              st + Cfg::oWCode + h * 8192 + row * 64 + ((j ^ ((row >> 1) & 3)) << 4));
+          const uint8_t* srow = st + Cfg::oWScale + h * 1024 + row * 8;
+          const uint32_t sc = *reinterpret_cast<const uint16_t*>(srow + j * 2);
+          uint2 T0, T1;
+          uint32_t e8;
+          scale_pair(ctl.tab, sc & 0xFFu, sc >> 8, T0, T1, e8);
+          uint32_t v[8];
+          nib8_to_e4m3(q.x, T0, v[0], v[1]);
+          nib8_to_e4m3(q.y, T0, v[2], v[3]);
+          nib8_to_e4m3(q.z, T1, v[4], v[5]);
+          nib8_to_e4m3(q.w, T1, v[6], v[7]);
+          tmem_st_x8(lane_base + Cfg::kACol0 + (s * KS + h) * 32 + j * 8, v);
+          const uint32_t sfw = Cfg::kSfCol0 + (s * KS + h) * Cfg::kSfColsPerChunk;
+          if (j == 0) {
+            // weight scales of this row's four K blocks -> column sfw + quarter
+            const uint2 all = *reinterpret_cast<const uint2*>(srow);
+            const uint32_t w = e8m0_of_pair(ctl.tab, all.x & 0xFFu, (all.x >> 8) & 0xFFu) |
+                               (e8m0_of_pair(ctl.tab, (all.x >> 16) & 0xFFu, all.x >> 24) << 8) |
+                               (e8m0_of_pair(ctl.tab, all.y & 0xFFu, (all.y >> 8) & 0xFFu) << 16) |
+                               (e8m0_of_pair(ctl.tab, (all.y >> 16) & 0xFFu, all.y >> 24) << 24);
+            tmem_st_x1(lane_base + sfw + quarter, w);
+          } else if (j == 1) {
+            // token scales, replicated in every lane quarter: token n = lane + 32c at column c
+            const uint32_t* raw = reinterpret_cast<const uint32_t*>(st + Cfg::oTokScale) + h * BN;
+            if constexpr (Cfg::kTokSfCols == 1) {
+              tmem_st_x1(lane_base + sfw + 4, lane < BN ? raw[lane] : 0u);
+            } else if constexpr (Cfg::kTokSfCols == 2) {
+              tmem_st_x2(lane_base + sfw + 4, raw[lane], raw[lane + 32]);
+            } else if constexpr (Cfg::kTokSfCols == 4) {
+              tmem_st_x4(lane_base + sfw + 4, raw[lane], raw[lane + 32], raw[lane + 64],
+                         raw[lane + 96]);
+            } else {
+              uint32_t t8[8];
+#pragma unroll
+              for (int c = 0; c < 8; ++c) t8[c] = raw[lane + 32 * c];
+              tmem_st_x8(lane_base + sfw + 4, t8);
+            }
+          }
         }
         tmem_st_wait();
-        fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&ctl.ready[s]));
@@ -372,6 +403,7 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
           tbase + buf * Cfg::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
       const int row = quarter * 32 + lane;
       bool finish = false;
+      int first = 0, last = -1;
       if (sg.slot >= 0) {
         // stream-K partial: store the slot, then count arrivals for this tile
         float* slot = p.slots + (static_cast<int64_t>(cta) * 2 + sg.slot) * (BN * 128);
@@ -384,10 +416,10 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
           for (int jj = 0; jj < 8; ++jj) __stcg(slot + (c0 + jj) * 128 + row, __uint_as_float(r[jj]));
         }
         __threadfence();
+        first = sch.cta_of(static_cast<int64_t>(sg.tile) * p.nks);
+        last = sch.cta_of(static_cast<int64_t>(sg.tile + 1) * p.nks - 1);
         named_barrier(1, 32 * Cfg::kEpiWarps);
         if (ep_tid == 0) {
-          const int first = sch.cta_of(static_cast<int64_t>(sg.tile) * p.nkt);
-          const int last = sch.cta_of(static_cast<int64_t>(sg.tile + 1) * p.nkt - 1);
           const uint32_t old = atomicAdd(p.counters + sg.tile, 1u);
           const bool fin = old == static_cast<uint32_t>(last - first);
           if (fin) p.counters[sg.tile] = 0;  // every contributor has arrived: rearm
@@ -396,11 +428,9 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
         named_barrier(1, 32 * Cfg::kEpiWarps);
         finish = ctl.bcast != 0;
         named_barrier(1, 32 * Cfg::kEpiWarps);
+        if (finish) __threadfence();
       }
       if (sg.slot < 0 || finish) {
-        const int first = sg.slot < 0 ? 0 : sch.cta_of(static_cast<int64_t>(sg.tile) * p.nkt);
-        const int last = sg.slot < 0 ? -1 : sch.cta_of(static_cast<int64_t>(sg.tile + 1) * p.nkt - 1);
-        if (finish) __threadfence();
         for (int c0 = 0; c0 < BN; c0 += 8) {
           if (c0 >= mcols) break;
           float acc[8];
@@ -414,8 +444,7 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
 #pragma unroll
             for (int jj = 0; jj < 8; ++jj) acc[jj] = 0.0f;
             for (int c = first; c <= last; ++c) {
-              const int64_t cu0 = sch.u0(c);
-              const int sl = (cu0 / p.nkt == sg.tile) ? 0 : 1;
+              const int sl = (sch.u0(c) / p.nks == sg.tile) ? 0 : 1;
               const float* slot = p.slots + (static_cast<int64_t>(c) * 2 + sl) * (BN * 128);
 #pragma unroll
               for (int jj = 0; jj < 8; ++jj) acc[jj] += __ldcg(slot + (c0 + jj) * 128 + row);
@@ -458,7 +487,7 @@ __global__ void __launch_bounds__(GemmCfg<BN>::kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
-    // tensor memory is freed only after every MMA / copy the MMA thread issued is done
+    // tensor memory is freed only after every MMA the MMA thread issued is done
     if (lane == 0) mbar_wait(smem_u32(&ctl.drain), 0, p.err, kErrWaitMma, nullptr);
     __syncwarp();
     tc_fence_after();

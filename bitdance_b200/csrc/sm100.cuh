@@ -22,14 +22,9 @@ enum : uint32_t {
   kErrShape = 1u << 8,       // the kernel saw a shape it does not support
 };
 
-// Wall-clock bound for any single wait (nanoseconds). Normal waits last microseconds.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
-
-__device__ __forceinline__ uint64_t globaltimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
+// Bound for any single wait, in SM clock cycles (about 2 s at 2 GHz). Normal waits last
+// microseconds.
+constexpr unsigned long long kWaitLimitCycles = 4000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -72,18 +67,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait on phase `parity`. On time-out ORs `code` into *err and *abort and
-// returns false. Also returns false early if another role already aborted.
+// returns false. Also returns false early if another role already aborted. The hot path is
+// a tight try_wait loop (try_wait itself suspends the thread in hardware for a while); the
+// abort flag and the cycle counter are looked at only every 1024 tries.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t* err,
                                           uint32_t code, volatile uint32_t* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  const long long t0 = clock64();
+  uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (abort_flag != nullptr && *abort_flag) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
-      if (err) atomicOr(err, code);
-      if (abort_flag) *abort_flag = 1u;
-      return false;
+    if ((++spins & 1023u) == 0) {
+      if (abort_flag != nullptr && *abort_flag) return false;
+      if (static_cast<unsigned long long>(clock64() - t0) > kWaitLimitCycles) {
+        if (err) atomicOr(err, code);
+        if (abort_flag) *abort_flag = 1u;
+        return false;
+      }
     }
   }
 }
@@ -166,6 +166,15 @@ __device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_st_x1(uint32_t taddr, uint32_t a) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(a)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_x2(uint32_t taddr, uint32_t a, uint32_t b) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1,%2};" ::"r"(taddr), "r"(a),
+               "r"(b)
+               : "memory");
 }
 __device__ __forceinline__ void tmem_st_x4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c,
                                            uint32_t d) {
