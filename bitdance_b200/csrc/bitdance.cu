@@ -331,8 +331,9 @@ int bd_w4a6_gemm(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8
   const int bn = token_tile(M);
   const int m_tiles = (M + bn - 1) / bn, n_tiles = N / 128;
   const int64_t tiles = static_cast<int64_t>(m_tiles) * n_tiles;
-  // stream-K for split_k == 0 unless atomics are asked for (they need no fix-up)
-  const bool streamk = split_k == 0 && split_mode != BD_SPLIT_ATOMIC;
+  // split_k == 0: stream-K when the tiles do not fill the machine twice over, whole tiles
+  // dealt round-robin otherwise (no fix-up needed); atomics never need the fix-up either
+  const bool streamk = split_k == 0 && split_mode != BD_SPLIT_ATOMIC && tiles < 2 * d->sm_count;
   if (split_k == 0 && !streamk) split_k = 1;
   const bool use_ws = split_k > 1 && split_mode == BD_SPLIT_REDUCE;
   StreamKSizes sk{0, 0, 0};

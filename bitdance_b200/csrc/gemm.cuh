@@ -47,8 +47,8 @@ constexpr int cpow2(int x) {
 template <int BN, int KS>
 struct GemmCfg {
   // KS 128-wide K chunks per pipeline stage
-  static constexpr int kStages = KS == 2 ? (BN >= 128 ? 3 : (BN >= 64 ? 4 : 5))
-                                         : (BN >= 256 ? 4 : (BN >= 128 ? 5 : 8));
+  static constexpr int kStages = KS == 2 ? (BN >= 64 ? 3 : (BN >= 32 ? 4 : 5))
+                                         : (BN >= 256 ? 4 : (BN >= 128 ? 5 : (BN >= 64 ? 6 : 8)));
   static constexpr int kTok = KS * BN * 128;     // token tiles (E2M3 operand image), SW128
   static constexpr int kWCode = KS * 128 * 64;   // packed NVFP4 codes, SW64
   static constexpr int kWScale = KS * 128 * 8;   // E4M3 per-16 scales
@@ -64,7 +64,10 @@ struct GemmCfg {
   // padded so every scale-factor address the MMA gets is a multiple of 4 columns
   static constexpr int kTokSfCols = BN >= 32 ? BN / 32 : 1;
   static constexpr int kSfColsPerChunk = 4 + cround(kTokSfCols, 4);
-  static constexpr int kAccCols = BN < 32 ? 32 : BN;
+  // narrow tiles alternate two accumulators along K so consecutive MMAs do not wait on
+  // each other's result; the epilogue adds them
+  static constexpr int kChains = BN <= 64 ? 2 : 1;
+  static constexpr int kAccCols = (kChains * BN) < 32 ? 32 : kChains * BN;
   static constexpr int kPerStageCols = KS * (32 + kSfColsPerChunk);
   static constexpr int kNumAcc = (2 * kAccCols + kStages * kPerStageCols <= 512) ? 2 : 1;
   static constexpr int kACol0 = kNumAcc * kAccCols;
@@ -110,10 +113,11 @@ struct Seg {
   int tile, k0, k1, z, slot;  // slot: -1 full tile, 0/1 stream-K partial slot
 };
 
-// The work of CTA `c` of `G`: segment number `idx` (false when there is none).
+// The work of CTA `c` of `G`: segment number `idx` (false when there is none). All indices
+// fit 32 bits (the host rejects larger problems).
 struct Schedule {
-  int64_t U;    // units (tile, stage)
-  int64_t q, r; // stream-K: U = q*G + r
+  int U;        // units (tile, stage)
+  int q, r;     // stream-K: U = q*G + r
   int G, nks, tiles, split;
 
   __device__ __forceinline__ void init(const GemmParams& p, int grid) {
@@ -121,38 +125,35 @@ struct Schedule {
     nks = p.nks;
     tiles = p.n_tiles * p.m_tiles;
     split = p.split_k;
-    U = static_cast<int64_t>(tiles) * nks;
+    U = tiles * nks;
     q = U / G;
     r = U % G;
   }
-  __device__ __forceinline__ int64_t u0(int c) const {
-    return c * q + (static_cast<int64_t>(c) < r ? static_cast<int64_t>(c) : r);
-  }
-  __device__ __forceinline__ int cta_of(int64_t u) const {
-    const int64_t big = r * (q + 1);
-    return u < big ? static_cast<int>(u / (q + 1)) : static_cast<int>(r + (u - big) / q);
+  __device__ __forceinline__ int u0(int c) const { return c * q + min(c, r); }
+  __device__ __forceinline__ int cta_of(int u) const {
+    const int big = r * (q + 1);
+    return u < big ? u / (q + 1) : r + (u - big) / q;
   }
   __device__ __forceinline__ bool segment(int c, int idx, Seg& s) const {
     if (split > 0) {
-      const int64_t item = c + static_cast<int64_t>(idx) * G;
-      if (item >= static_cast<int64_t>(tiles) * split) return false;
-      s.tile = static_cast<int>(item / split);
-      s.z = static_cast<int>(item % split);
+      const int item = c + idx * G;
+      if (item >= tiles * split) return false;
+      s.tile = item / split;
+      s.z = item % split;
       const int per = nks / split;
       s.k0 = s.z * per;
       s.k1 = s.k0 + per;
       s.slot = -1;
       return true;
     }
-    const int64_t a = u0(c), b = u0(c + 1);
+    const int a = u0(c), b = u0(c + 1);
     if (a >= b) return false;
-    const int64_t t = a / nks + idx;
-    const int64_t lo = a > t * nks ? a : t * nks;
-    const int64_t hi = b < (t + 1) * nks ? b : (t + 1) * nks;
+    const int t = a / nks + idx;
+    const int lo = max(a, t * nks), hi = min(b, (t + 1) * nks);
     if (lo >= hi) return false;
-    s.tile = static_cast<int>(t);
-    s.k0 = static_cast<int>(lo - t * nks);
-    s.k1 = static_cast<int>(hi - t * nks);
+    s.tile = t;
+    s.k0 = lo - t * nks;
+    s.k1 = hi - t * nks;
     s.z = 0;
     s.slot = (s.k0 == 0 && s.k1 == nks) ? -1 : (idx == 0 ? 0 : 1);
     return true;
@@ -308,8 +309,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, KS>::kThreads, 1)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               const uint32_t idesc = idesc_mxf8f6f4(128, BN, kFmtE4M3, kFmtE2M3, kk, kk);
-              mma_mxf8f6f4_ts(tD, tA + kk * 8, sdesc_sw128(ab + kk * 32), idesc, tSfW, tSfA,
-                              (k > sg.k0 || h > 0 || kk > 0) ? 1u : 0u);
+              const int chain = kk % Cfg::kChains;
+              const bool first = (k == sg.k0 && h == 0 && kk < Cfg::kChains);
+              mma_mxf8f6f4_ts(tD + chain * BN, tA + kk * 8, sdesc_sw128(ab + kk * 32), idesc,
+                              tSfW, tSfA, first ? 0u : 1u);
             }
           }
           tc_commit(smem_u32(&ctl.empty[s]));
@@ -322,12 +325,15 @@ __global__ void __launch_bounds__(GemmCfg<BN, KS>::kThreads, 1)
     }
   } else if (warp >= 2 + Cfg::kEpiWarps) {
     // ------------------------------------------------------------------ transcode
+    // Software-pipelined by one stage: the tensor-memory stores of stage i drain while stage
+    // i+1 is loaded and converted; only then does the warp wait for them and signal ready(i).
+    // (Stage i+1's data never depends on ready(i): the producer is S >= 2 stages ahead.)
     const int tw = warp - 2 - Cfg::kEpiWarps;   // 0..15
     const int quarter = warp & 3;               // TMEM lane quarter this warp may access
     const int j = tw >> 2;                      // K block (32 elements) of each chunk
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
-    int i = 0;
+    int i = 0, prev = -1;
     Seg sg;
     for (int idx = 0; sch.segment(cta, idx, sg) && !*abort_flag; ++idx) {
       for (int k = sg.k0; k < sg.k1; ++k, ++i) {
@@ -335,6 +341,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, KS>::kThreads, 1)
         const uint32_t ph = (i / S) & 1;
         if (!mbar_wait(smem_u32(&ctl.full[s]), ph, p.err, kErrWaitTma, abort_flag)) break;
         const uint8_t* st = smem + s * Cfg::kStageBytes;
+        uint32_t v[KS][8];
+        uint32_t sfw_word[KS];
+        uint32_t tok[KS][Cfg::kTokSfCols];
 #pragma unroll
         for (int h = 0; h < KS; ++h) {
           // 64B-swizzled codes: 16-byte chunk c of row r at r*64 + (c ^ ((r >> 1) & 3)) * 16
@@ -345,47 +354,65 @@ __global__ void __launch_bounds__(GemmCfg<BN, KS>::kThreads, 1)
           uint2 T0, T1;
           uint32_t e8;
           scale_pair(ctl.tab, sc & 0xFFu, sc >> 8, T0, T1, e8);
-          uint32_t v[8];
-          nib8_to_e4m3(q.x, T0, v[0], v[1]);
-          nib8_to_e4m3(q.y, T0, v[2], v[3]);
-          nib8_to_e4m3(q.z, T1, v[4], v[5]);
-          nib8_to_e4m3(q.w, T1, v[6], v[7]);
-          tmem_st_x8(lane_base + Cfg::kACol0 + (s * KS + h) * 32 + j * 8, v);
+          nib8_to_e4m3(q.x, T0, v[h][0], v[h][1]);
+          nib8_to_e4m3(q.y, T0, v[h][2], v[h][3]);
+          nib8_to_e4m3(q.z, T1, v[h][4], v[h][5]);
+          nib8_to_e4m3(q.w, T1, v[h][6], v[h][7]);
+          if (j == 0) {
+            // weight scales of this row's four K blocks, one word for column sfw + quarter
+            const uint2 all = *reinterpret_cast<const uint2*>(srow);
+            sfw_word[h] = e8m0_of_pair(ctl.tab, all.x & 0xFFu, (all.x >> 8) & 0xFFu) |
+                          (e8m0_of_pair(ctl.tab, (all.x >> 16) & 0xFFu, all.x >> 24) << 8) |
+                          (e8m0_of_pair(ctl.tab, all.y & 0xFFu, (all.y >> 8) & 0xFFu) << 16) |
+                          (e8m0_of_pair(ctl.tab, (all.y >> 16) & 0xFFu, all.y >> 24) << 24);
+          } else if (j == 1) {
+            // token scales: token n = lane + 32c at column c, in every lane quarter
+            const uint32_t* raw = reinterpret_cast<const uint32_t*>(st + Cfg::oTokScale) + h * BN;
+#pragma unroll
+            for (int c = 0; c < Cfg::kTokSfCols; ++c)
+              tok[h][c] = (lane + 32 * c < BN) ? raw[lane + 32 * c] : 0u;
+          }
+        }
+        if (prev >= 0) {
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&ctl.ready[prev]));
+        }
+#pragma unroll
+        for (int h = 0; h < KS; ++h) {
+          tmem_st_x8(lane_base + Cfg::kACol0 + (s * KS + h) * 32 + j * 8, v[h]);
           const uint32_t sfw = Cfg::kSfCol0 + (s * KS + h) * Cfg::kSfColsPerChunk;
           if (j == 0) {
-            // weight scales of this row's four K blocks -> column sfw + quarter
-            const uint2 all = *reinterpret_cast<const uint2*>(srow);
-            const uint32_t w = e8m0_of_pair(ctl.tab, all.x & 0xFFu, (all.x >> 8) & 0xFFu) |
-                               (e8m0_of_pair(ctl.tab, (all.x >> 16) & 0xFFu, all.x >> 24) << 8) |
-                               (e8m0_of_pair(ctl.tab, all.y & 0xFFu, (all.y >> 8) & 0xFFu) << 16) |
-                               (e8m0_of_pair(ctl.tab, (all.y >> 16) & 0xFFu, all.y >> 24) << 24);
-            tmem_st_x1(lane_base + sfw + quarter, w);
+            tmem_st_x1(lane_base + sfw + quarter, sfw_word[h]);
           } else if (j == 1) {
-            // token scales, replicated in every lane quarter: token n = lane + 32c at column c
-            const uint32_t* raw = reinterpret_cast<const uint32_t*>(st + Cfg::oTokScale) + h * BN;
             if constexpr (Cfg::kTokSfCols == 1) {
-              tmem_st_x1(lane_base + sfw + 4, lane < BN ? raw[lane] : 0u);
+              tmem_st_x1(lane_base + sfw + 4, tok[h][0]);
             } else if constexpr (Cfg::kTokSfCols == 2) {
-              tmem_st_x2(lane_base + sfw + 4, raw[lane], raw[lane + 32]);
+              tmem_st_x2(lane_base + sfw + 4, tok[h][0], tok[h][1]);
             } else if constexpr (Cfg::kTokSfCols == 4) {
-              tmem_st_x4(lane_base + sfw + 4, raw[lane], raw[lane + 32], raw[lane + 64],
-                         raw[lane + 96]);
+              tmem_st_x4(lane_base + sfw + 4, tok[h][0], tok[h][1], tok[h][2], tok[h][3]);
             } else {
               uint32_t t8[8];
 #pragma unroll
-              for (int c = 0; c < 8; ++c) t8[c] = raw[lane + 32 * c];
+              for (int c = 0; c < 8; ++c) t8[c] = tok[h][c % Cfg::kTokSfCols];
               tmem_st_x8(lane_base + sfw + 4, t8);
             }
           }
         }
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&ctl.ready[s]));
+        prev = s;
       }
+    }
+    if (prev >= 0) {
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&ctl.ready[prev]));
     }
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..5)
+    // accumulator columns per tensor-memory load
+    constexpr int kB = (BN < 32 || Cfg::kChains == 2) ? 16 : 32;
     const int quarter = warp & 3;
     const int ep_tid = tid - 64;  // 0..127
     Seg sg;
@@ -402,22 +429,37 @@ __global__ void __launch_bounds__(GemmCfg<BN, KS>::kThreads, 1)
       const uint32_t taddr =
           tbase + buf * Cfg::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
       const int row = quarter * 32 + lane;
+      // accumulator columns [c0, c0 + kB) of this thread's row, chains added
+      auto load_acc = [&](int c0, float (&acc)[kB]) {
+        uint32_t r[kB];
+        if constexpr (kB == 16) tmem_ld_x16(taddr + c0, r); else tmem_ld_x32(taddr + c0, r);
+        if constexpr (Cfg::kChains == 2) {
+          uint32_t r2[kB];
+          if constexpr (kB == 16) tmem_ld_x16(taddr + BN + c0, r2);
+          else tmem_ld_x32(taddr + BN + c0, r2);
+          tmem_ld_wait();
+#pragma unroll
+          for (int jj = 0; jj < kB; ++jj) acc[jj] = __uint_as_float(r[jj]) + __uint_as_float(r2[jj]);
+        } else {
+          tmem_ld_wait();
+#pragma unroll
+          for (int jj = 0; jj < kB; ++jj) acc[jj] = __uint_as_float(r[jj]);
+        }
+      };
       bool finish = false;
       int first = 0, last = -1;
       if (sg.slot >= 0) {
         // stream-K partial: store the slot, then count arrivals for this tile
         float* slot = p.slots + (static_cast<int64_t>(cta) * 2 + sg.slot) * (BN * 128);
-        for (int c0 = 0; c0 < BN; c0 += 8) {
-          if (c0 >= mcols) break;
-          uint32_t r[8];
-          tmem_ld_x8(taddr + c0, r);
-          tmem_ld_wait();
+        for (int c0 = 0; c0 < mcols; c0 += kB) {
+          float acc[kB];
+          load_acc(c0, acc);
 #pragma unroll
-          for (int jj = 0; jj < 8; ++jj) __stcg(slot + (c0 + jj) * 128 + row, __uint_as_float(r[jj]));
+          for (int jj = 0; jj < kB; ++jj) __stcg(slot + (c0 + jj) * 128 + row, acc[jj]);
         }
         __threadfence();
-        first = sch.cta_of(static_cast<int64_t>(sg.tile) * p.nks);
-        last = sch.cta_of(static_cast<int64_t>(sg.tile + 1) * p.nks - 1);
+        first = sch.cta_of(sg.tile * p.nks);
+        last = sch.cta_of((sg.tile + 1) * p.nks - 1);
         named_barrier(1, 32 * Cfg::kEpiWarps);
         if (ep_tid == 0) {
           const uint32_t old = atomicAdd(p.counters + sg.tile, 1u);
@@ -431,27 +473,32 @@ __global__ void __launch_bounds__(GemmCfg<BN, KS>::kThreads, 1)
         if (finish) __threadfence();
       }
       if (sg.slot < 0 || finish) {
-        for (int c0 = 0; c0 < BN; c0 += 8) {
-          if (c0 >= mcols) break;
-          float acc[8];
-          if (sg.slot < 0) {
-            uint32_t r[8];
-            tmem_ld_x8(taddr + c0, r);
-            tmem_ld_wait();
+        for (int c0 = 0; c0 < mcols; c0 += kB) {
+          float acc[kB];
+          load_acc(c0, acc);   // this CTA's own part straight from tensor memory
+          if (finish) {
+            // add the contributors in CTA order (own part in its place): the result does not
+            // depend on which CTA happened to arrive last
+            float own[kB];
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj) acc[jj] = __uint_as_float(r[jj]);
-          } else {
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj) acc[jj] = 0.0f;
+            for (int jj = 0; jj < kB; ++jj) {
+              own[jj] = acc[jj];
+              acc[jj] = 0.0f;
+            }
             for (int c = first; c <= last; ++c) {
+              if (c == cta) {
+#pragma unroll
+                for (int jj = 0; jj < kB; ++jj) acc[jj] += own[jj];
+                continue;
+              }
               const int sl = (sch.u0(c) / p.nks == sg.tile) ? 0 : 1;
               const float* slot = p.slots + (static_cast<int64_t>(c) * 2 + sl) * (BN * 128);
 #pragma unroll
-              for (int jj = 0; jj < 8; ++jj) acc[jj] += __ldcg(slot + (c0 + jj) * 128 + row);
+              for (int jj = 0; jj < kB; ++jj) acc[jj] += __ldcg(slot + (c0 + jj) * 128 + row);
             }
           }
 #pragma unroll
-          for (int jj = 0; jj < 8; ++jj) {
+          for (int jj = 0; jj < kB; ++jj) {
             const int m = m0 + c0 + jj;
             if (c0 + jj < mcols) {
               const float a = acc[jj];
