@@ -231,12 +231,15 @@ def run_ours(args, rank, world, local_rank):
         raise RuntimeError("kernel error word set")
 
     stream = torch.cuda.Stream(device=dev)
+    # consecutive GEMMs overlap: each may start streaming its (static) weights while the
+    # previous one finishes; A, C and the workspace wait for the previous kernel
+    ov = not args.no_overlap
 
     def step_kernels():
         for M in M_SWEEP:
             for w in weights:
                 ops.w4a6_gemm(acts[M], w, out=outs[M], split_k=splits[M], workspace=wss[M],
-                              stream=stream)
+                              stream=stream, overlap_prev=ov, weights_static=ov)
 
     # e2e: pinned host inputs -> device, pack (public API), GEMMs, device -> pinned host outputs
     h_in = {M: (torch.empty((M, K_W), dtype=torch.uint8).pin_memory(),
@@ -258,7 +261,7 @@ def run_ours(args, rank, world, local_rank):
             e2e_acts[M] = a
             for w in weights:
                 ops.w4a6_gemm(a, w, out=outs[M], split_k=splits[M], workspace=wss[M],
-                              stream=stream)
+                              stream=stream, overlap_prev=ov, weights_static=ov)
             h_out[M].copy_(outs[M], non_blocking=True)
 
     def capture(fn):
@@ -332,7 +335,8 @@ def run_ours(args, rank, world, local_rank):
                    "l2": f"{LAYERS} weight matrices per rank ({LAYERS * weight_bytes(N_W, K_W) / 1e6:.0f} MB) "
                          "rotate, larger than the 126 MB L2",
                    "parallelism": f"N-sharded x{world}, no collective in the timed region",
-                   "launch": "CUDA graph of one step"},
+                   "launch": "CUDA graph of one step" + (
+                       ", programmatic serialisation between GEMMs" if ov else "")},
         "tflops": flops_step * args.steps / (ms_k / 1e3) / 1e12 * world,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "peak_kind": peak_kind,
@@ -401,11 +405,15 @@ def run_case(args):
     g = torch.Generator(device=dev)
     g.manual_seed(7)
     if args.case == "gemm":
+        # weight matrices rotate so the working set exceeds the 126 MB L2; the calls are
+        # captured in one CUDA graph so the time is device time, not host launch overhead
         M, N, K = args.M, args.N, args.K
-        w = ops.pack_weights(torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev,
-                                           generator=g),
-                             torch.randint(0x58, 0x7F, (N, K // 16), dtype=torch.uint8,
-                                           device=dev, generator=g), 1.0)
+        reps = max(2, -(-300_000_000 // weight_bytes(N, K)))
+        ws_list = [ops.pack_weights(torch.randint(0, 256, (N, K // 2), dtype=torch.uint8,
+                                                  device=dev, generator=g),
+                                    torch.randint(0x58, 0x7F, (N, K // 16), dtype=torch.uint8,
+                                                  device=dev, generator=g), 1.0)
+                   for _ in range(reps)]
         a = ops.pack_activations(torch.randint(0, 64, (M, K), dtype=torch.uint8, device=dev,
                                                generator=g),
                                  torch.randint(120, 135, (M, K // 32), dtype=torch.uint8,
@@ -413,8 +421,22 @@ def run_case(args):
         out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
         split = args.split
         wsp = ops.Workspace()
-        fn = lambda: ops.w4a6_gemm(a, w, out=out, split_k=split, workspace=wsp)  # noqa: E731
-        work = {"M": M, "N": N, "K": K, "split_k": split,
+        stream = torch.cuda.Stream(device=dev)
+        ov = bool(args.overlap)
+
+        def body():
+            for i in range(args.steps):
+                ops.w4a6_gemm(a, ws_list[i % reps], out=out, split_k=split, workspace=wsp,
+                              stream=stream, overlap_prev=ov, weights_static=ov)
+        with torch.cuda.stream(stream):
+            body()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            body()
+        fn = graph.replay  # noqa: E731
+        calls = args.steps
+        work = {"M": M, "N": N, "K": K, "split_k": split, "overlap": ov, "rotating_weights": reps,
                 "weight_bytes": weight_bytes(N, K), "flops": 2 * M * N * K}
     else:
         nblk = args.nblk
@@ -422,19 +444,24 @@ def run_case(args):
         sc = torch.randint(0x01, 0x7F, (nblk * 2,), dtype=torch.uint8, device=dev, generator=g)
         e6 = torch.empty(nblk * 32, dtype=torch.uint8, device=dev)
         e8 = torch.empty(nblk, dtype=torch.uint8, device=dev)
+        stream = torch.cuda.current_stream()
         fn = lambda: ops.transcode(codes, sc, 16, e2m3=e6, e8m0=e8)  # noqa: E731
+        calls = 1
         work = {"nblk32": nblk, "bytes": nblk * (16 + 2 + 32 + 1)}
-    for _ in range(args.warmup):
-        fn()
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup if args.case != "gemm" else 3)):
+            fn()
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(args.steps):
-        fn()
-    t1.record()
+    reps_t = 3 if args.case == "gemm" else args.steps
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(reps_t):
+            fn()
+        t1.record(stream)
     torch.cuda.synchronize()
-    us = t0.elapsed_time(t1) * 1e3 / args.steps
+    us = t0.elapsed_time(t1) * 1e3 / (reps_t * calls)
     res = {"case": args.case, "us_per_call": us, **work}
     if args.case == "gemm":
         res["weight_gbs"] = work["weight_bytes"] / us / 1e3
@@ -455,6 +482,8 @@ def main():
     ap.add_argument("--N", type=int, default=14336)
     ap.add_argument("--K", type=int, default=4096)
     ap.add_argument("--split", type=int, default=0)
+    ap.add_argument("--overlap", type=int, default=1,
+                    help="--case gemm: launch with programmatic serialisation (weights static)")
     ap.add_argument("--nblk", type=int, default=1 << 26)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
@@ -463,6 +492,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="launch every GEMM only after the previous kernel completed")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

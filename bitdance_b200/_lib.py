@@ -25,6 +25,7 @@ BD_ERR_DEVICE = -7
 BD_OUT_BF16, BD_OUT_F16, BD_OUT_F32 = 0, 1, 2
 BD_EPI_NONE, BD_EPI_BIAS, BD_EPI_BIAS_RELU, BD_EPI_BIAS_SILU, BD_EPI_BIAS_GELU = 0, 1, 2, 3, 4
 BD_SPLIT_REDUCE, BD_SPLIT_PLANES, BD_SPLIT_ATOMIC = 0, 1, 2
+BD_GEMM_OVERLAP_PREV, BD_GEMM_WEIGHTS_STATIC = 1, 2
 
 # name -> (restype, argtypes); mirrors include/bitdance_b200.h
 _P = ctypes.c_void_p
@@ -41,6 +42,8 @@ SIGNATURES = {
     "bd_pack_a": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "bd_query_workspace": (_SZ, [_I, _I, _I, _I, _I]),
     "bd_w4a6_gemm": (_I, [_P, _P, _P, _P, _P, _F, _P, _I, _I, _I, _I, _I, _I, _I, _P, _SZ, _P]),
+    "bd_w4a6_gemm_ex": (_I, [_P, _P, _P, _P, _P, _F, _P, _I, _I, _I, _I, _I, _I, _I, _P, _SZ,
+                             ctypes.c_uint, _P]),
     "bd_splitk_reduce": (_I, [_P, _P, _P, _F, _I, _I, _I, _I, _I, _P]),
 }
 

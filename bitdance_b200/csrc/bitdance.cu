@@ -110,27 +110,28 @@ int grid_for(int64_t work, int per_block, const DeviceInfo* d) {
   return static_cast<int>(blocks < 1 ? 1 : blocks);
 }
 
+// Token rows loaded per tile (the MMA's M operand is 128 rows; a decode batch loads fewer).
 int token_tile(int M) {
   if (M <= 16) return 16;
   if (M <= 32) return 32;
   if (M <= 64) return 64;
-  if (M <= 128) return 128;
-  return 256;
+  return 128;
 }
 
-// Stream-K scratch of one call: per-CTA partial slots [grid][2][BN][128] fp32, then one
+// Stream-K scratch of one call: per-CTA partial slots [grid][2][BM][256] fp32, then one
 // arrival counter per tile. Counters must be zero before the first call; every call leaves
 // them zero again.
 struct StreamKSizes {
   size_t slots_bytes, counter_bytes, total;
 };
 StreamKSizes streamk_sizes(int M, int N, int K, int sm_count) {
-  const int bn = token_tile(M);
-  const int64_t tiles = static_cast<int64_t>(N / 128) * ((M + bn - 1) / bn);
+  const int bm = token_tile(M);
+  const int64_t tiles = static_cast<int64_t>((N + kTileN - 1) / kTileN) * ((M + bm - 1) / bm);
   const int64_t units = tiles * (K / 128);
   const int64_t grid = units < sm_count ? units : sm_count;
   StreamKSizes z;
-  z.slots_bytes = (static_cast<size_t>(grid) * 2 * bn * 128 * sizeof(float) + 255) / 256 * 256;
+  z.slots_bytes =
+      (static_cast<size_t>(grid) * 2 * bm * kTileN * sizeof(float) + 255) / 256 * 256;
   z.counter_bytes = (static_cast<size_t>(tiles) * sizeof(uint32_t) + 255) / 256 * 256;
   z.total = z.slots_bytes + z.counter_bytes;
   return z;
@@ -140,41 +141,42 @@ struct GemmMaps {
   CUtensorMap a, as, w, ws;
 };
 
-template <int BN, int KS>
-int launch_gemm(const GemmMaps& m, const GemmParams& p, int grid, cudaStream_t stream) {
-  using Cfg = GemmCfg<BN, KS>;
+template <int BM>
+int launch_gemm(const GemmMaps& m, const GemmParams& p, int grid, bool overlap,
+                cudaStream_t stream) {
+  using Cfg = GemmCfg<BM>;
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load() & bit)) {
-    if (cudaFuncSetAttribute(w4a6_gemm_kernel<BN, KS>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(w4a6_gemm_kernel<BM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Cfg::kSmemBytes) != cudaSuccess)
       return BD_ERR_CUDA;
     configured.fetch_or(bit);
   }
-  w4a6_gemm_kernel<BN, KS><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(m.a, m.as, m.w,
-                                                                              m.ws, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(Cfg::kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = overlap ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, w4a6_gemm_kernel<BM>, m.a, m.as, m.w, m.ws, p) != cudaSuccess)
+    return BD_ERR_CUDA;
   return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
 }
 
-int launch_gemm_any(int bn, int ks, const GemmMaps& m, const GemmParams& p, int grid,
+int launch_gemm_any(int bm, const GemmMaps& m, const GemmParams& p, int grid, bool overlap,
                     cudaStream_t s) {
-  if (ks == 2) {
-    switch (bn) {
-      case 16: return launch_gemm<16, 2>(m, p, grid, s);
-      case 32: return launch_gemm<32, 2>(m, p, grid, s);
-      case 64: return launch_gemm<64, 2>(m, p, grid, s);
-      default: return launch_gemm<128, 2>(m, p, grid, s);
-    }
-  }
-  switch (bn) {
-    case 16: return launch_gemm<16, 1>(m, p, grid, s);
-    case 32: return launch_gemm<32, 1>(m, p, grid, s);
-    case 64: return launch_gemm<64, 1>(m, p, grid, s);
-    case 128: return launch_gemm<128, 1>(m, p, grid, s);
-    default: return launch_gemm<256, 1>(m, p, grid, s);
+  switch (bm) {
+    case 16: return launch_gemm<16>(m, p, grid, overlap, s);
+    case 32: return launch_gemm<32>(m, p, grid, overlap, s);
+    case 64: return launch_gemm<64>(m, p, grid, overlap, s);
+    default: return launch_gemm<128>(m, p, grid, overlap, s);
   }
 }
 
@@ -308,6 +310,16 @@ int bd_w4a6_gemm(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8
                  const uint8_t* b_scales, float b_tensor_scale, const void* bias, int M, int N,
                  int K, int split_k, int split_mode, int out_dtype, int epilogue, void* workspace,
                  size_t workspace_bytes, bd_stream_t stream) {
+  return bd_w4a6_gemm_ex(c, a, a_scales, b, b_scales, b_tensor_scale, bias, M, N, K, split_k,
+                         split_mode, out_dtype, epilogue, workspace, workspace_bytes, 0u, stream);
+}
+
+int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8_t* b,
+                    const uint8_t* b_scales, float b_tensor_scale, const void* bias, int M, int N,
+                    int K, int split_k, int split_mode, int out_dtype, int epilogue,
+                    void* workspace, size_t workspace_bytes, unsigned flags, bd_stream_t stream) {
+  if (flags & ~static_cast<unsigned>(BD_GEMM_OVERLAP_PREV | BD_GEMM_WEIGHTS_STATIC))
+    return BD_ERR_INVALID_ARG;
   if (!c || !a || !a_scales || !b || !b_scales) return BD_ERR_INVALID_ARG;
   if (out_dtype < BD_OUT_BF16 || out_dtype > BD_OUT_F32) return BD_ERR_INVALID_ARG;
   if (epilogue < BD_EPI_NONE || epilogue > BD_EPI_BIAS_GELU) return BD_ERR_INVALID_ARG;
@@ -328,8 +340,8 @@ int bd_w4a6_gemm(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8
   int st = device_info(&d);
   if (st != BD_OK) return st;
 
-  const int bn = token_tile(M);
-  const int m_tiles = (M + bn - 1) / bn, n_tiles = N / 128;
+  const int bm = token_tile(M);
+  const int m_tiles = (M + bm - 1) / bm, n_tiles = (N + kTileN - 1) / kTileN;
   const int64_t tiles = static_cast<int64_t>(m_tiles) * n_tiles;
   // split_k == 0: stream-K when the tiles do not fill the machine twice over, whole tiles
   // dealt round-robin otherwise (no fix-up needed); atomics never need the fix-up either
@@ -348,22 +360,19 @@ int bd_w4a6_gemm(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8
     if (!aligned(workspace, 16) || N % 4) return BD_ERR_ALIGNMENT;
   }
 
-  // pipeline stages of two 128-wide K chunks when the shape allows it
-  const int ks = (bn <= 128 && nkt % 2 == 0 && (split_k == 0 || (nkt / 2) % split_k == 0)) ? 2 : 1;
-  const int nks = nkt / ks;
   const int Mp4 = (M + 3) / 4 * 4;
   GemmMaps maps;
   if (!make_map_3d(&maps.a, CU_TENSOR_MAP_DATA_TYPE_UINT8, const_cast<uint8_t*>(a), 128, M, nkt,
-                   K, 128, 128, bn, ks, CU_TENSOR_MAP_SWIZZLE_128B))
+                   K, 128, 128, bm, 1, CU_TENSOR_MAP_SWIZZLE_128B))
     return BD_ERR_CUDA;
   if (!make_map_2d(&maps.as, CU_TENSOR_MAP_DATA_TYPE_UINT32, const_cast<uint8_t*>(a_scales), Mp4,
-                   nkt, static_cast<uint64_t>(Mp4) * 4, bn, ks, CU_TENSOR_MAP_SWIZZLE_NONE))
+                   nkt, static_cast<uint64_t>(Mp4) * 4, bm, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
     return BD_ERR_CUDA;
   if (!make_map_2d(&maps.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, const_cast<uint8_t*>(b), 64,
-                   static_cast<uint64_t>(N) * nkt, 64, 64, 128 * ks, CU_TENSOR_MAP_SWIZZLE_64B))
+                   static_cast<uint64_t>(N) * nkt, 64, 64, 128, CU_TENSOR_MAP_SWIZZLE_64B))
     return BD_ERR_CUDA;
   if (!make_map_2d(&maps.ws, CU_TENSOR_MAP_DATA_TYPE_UINT32, const_cast<uint8_t*>(b_scales), 256,
-                   static_cast<uint64_t>(n_tiles) * nkt, 1024, 256, ks, CU_TENSOR_MAP_SWIZZLE_NONE))
+                   static_cast<uint64_t>(N / 128) * nkt, 1024, 256, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
     return BD_ERR_CUDA;
 
   GemmParams p;
@@ -374,10 +383,13 @@ int bd_w4a6_gemm(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8
   p.K = K;
   p.n_tiles = n_tiles;
   p.m_tiles = m_tiles;
-  p.nks = nks;
+  p.nks = nkt;
+  p.n_half_tiles = N / 128;
   p.split_k = streamk ? 0 : split_k;
   p.out_dtype = out_dtype;
   p.epilogue = epilogue;
+  p.weights_early = (flags & BD_GEMM_WEIGHTS_STATIC) ? 1 : 0;
+  p.vec_out = aligned(c, 16) ? 1 : 0;
   p.err = d->err;
   p.slots = nullptr;
   p.counters = nullptr;
@@ -388,13 +400,14 @@ int bd_w4a6_gemm(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8
     p.split_out = kOutPartial;
     p.out = workspace;
   } else p.split_out = kOutPlane;
-  const int64_t work = streamk ? tiles * nks : tiles * split_k;
+  const int64_t work = streamk ? tiles * nkt : tiles * split_k;
   if (streamk) {
     p.slots = static_cast<float*>(workspace);
     p.counters = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + sk.slots_bytes);
   }
   const int grid = static_cast<int>(work < d->sm_count ? work : d->sm_count);
-  const int rc = launch_gemm_any(bn, ks, maps, p, grid, as_stream(stream));
+  const int rc = launch_gemm_any(bm, maps, p, grid, (flags & BD_GEMM_OVERLAP_PREV) != 0,
+                                 as_stream(stream));
   if (rc != BD_OK || !use_ws) return rc;
   return bd_splitk_reduce(static_cast<const float*>(workspace), c, bias, b_tensor_scale, M, N,
                           split_k, out_dtype, epilogue, stream);

@@ -1,7 +1,10 @@
 // gemm.cuh -- fused W4A6 GEMM for sm_100a: C = A_mxfp6 . transcode(B_nvfp4)^T.
 //
-// Tiles of C^T: 128 weight rows (N, the MMA's M operand) x BN tokens (M, the MMA's N
-// operand), so a decode batch of a few tokens still fills 128-row MMAs.
+// One block-scaled tcgen05.mma (kind::mxf8f6f4, M = 128, K = 32) costs the tensor core the
+// same time whatever its N (16..256), so the weights are the MMA's N operand, 256 rows per
+// MMA, and the tokens are its M operand (128 rows; a decode batch loads only its BM <= 128
+// token rows and leaves the rest of the operand unused). Output tile: BM tokens x 256 weight
+// rows, accumulated in tensor memory as 128 lanes (tokens) x 256 fp32 columns (weight rows).
 //
 // Persistent CTAs walk a schedule of "segments" (a tile and a range of 128-wide K chunks):
 //   * stream-K (the default): the (tile, K chunk) units are cut into one contiguous range per
@@ -11,17 +14,20 @@
 //   * explicit split-K (split_k >= 1): items (tile, split) dealt round-robin, written as
 //     partial planes, fp32 workspace planes or fp32 atomics (the reference's split modes).
 //
-// Warp roles (704 threads):
-//   warp 0      producer   TMA: packed NVFP4 codes (8 KB, 64B-swizzled), E4M3 scales (1 KB),
-//                          token tile (128B-swizzled), token E8M0 scales; one mbarrier/stage.
-//   warps 6..21 transcode  16 warps; warp (quarter q, K block j) turns rows 32q..32q+31 x
-//                          32 K-elements into E4M3 bytes in tensor memory (tcgen05.st; the
-//                          MMA reads its A operand from there) and their E8M0 scales.
-//   warp 1      MMA        tcgen05.cp of both scale blocks, 4 block-scaled tcgen05.mma
-//                          (kind::mxf8f6f4, A from TMEM, K = 32 each), commit frees the stage.
-//   warps 2..5  epilogue   TMEM accumulator -> registers -> C / partials (double-buffered
-//                          accumulators when tensor memory allows, so it overlaps the next
-//                          segment's main loop).
+// Warp roles (736 threads):
+//   warp 0      weight producer  TMA: packed NVFP4 codes (2 x 8 KB per chunk, 64B-swizzled)
+//                                and E4M3 scales (2 x 1 KB) into the weight ring (deep).
+//   warp 22     token producer   TMA: token rows (128B-swizzled packed E2M3) and their E8M0
+//                                scales into the token ring.
+//   warps 6..21 transcode        16 warps; thread (warp w, lane l) converts weight row
+//                                16w + (l & 15), K blocks 2(l >> 4) and 2(l >> 4) + 1 of a
+//                                chunk into E4M3 bytes of the 128B-swizzled operand tile in
+//                                shared memory (the B ring) and stages the row's E8M0 scales.
+//   warp 1      MMA              4 block-scaled tcgen05.mma per chunk (both operands from
+//                                shared memory); its commits free the B and token slots.
+//   warps 2..5  epilogue         per chunk: token and weight scale factors into tensor memory
+//                                (tcgen05.st, one warp per lane quarter); per segment:
+//                                tensor-memory accumulator -> registers -> C / partials.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -38,57 +44,67 @@ enum : int {
 };
 
 constexpr int cround(int x, int a) { return (x + a - 1) / a * a; }
-constexpr int cpow2(int x) {
-  int p = 32;
-  while (p < x) p *= 2;
-  return p;
+
+constexpr int kTileN = 256;  // weight rows per tile (the MMA's N)
+
+// Ring depths per token rows BM: weight ring SW (raw NVFP4, released by the transcode warps
+// once in registers), B ring SB (transcoded operand, released by the MMA), token ring ST.
+struct RingDepths {
+  int sw, sb, st;
+};
+constexpr RingDepths ring_depths(int BM) {
+  if (BM <= 16) return {6, 3, 4};
+  if (BM <= 32) return {5, 3, 4};
+  if (BM <= 64) return {5, 3, 3};
+  return {4, 3, 3};
 }
 
-template <int BN, int KS>
+template <int BM>
 struct GemmCfg {
-  // KS 128-wide K chunks per pipeline stage
-  static constexpr int kStages = KS == 2 ? (BN >= 64 ? 3 : (BN >= 32 ? 4 : 5))
-                                         : (BN >= 256 ? 4 : (BN >= 128 ? 5 : (BN >= 64 ? 6 : 8)));
-  static constexpr int kTok = KS * BN * 128;     // token tiles (E2M3 operand image), SW128
-  static constexpr int kWCode = KS * 128 * 64;   // packed NVFP4 codes, SW64
-  static constexpr int kWScale = KS * 128 * 8;   // E4M3 per-16 scales
-  static constexpr int kTokScale = cround(KS * BN * 4, 128);
-  static constexpr int oTok = 0;
-  static constexpr int oWCode = cround(oTok + kTok, 1024);
-  static constexpr int oWScale = oWCode + kWCode;
-  static constexpr int oTokScale = oWScale + kWScale;
-  static constexpr int kStageBytes = cround(oTokScale + kTokScale, 1024);
-  static constexpr int kTxBytes = kWCode + kWScale + kTok + KS * BN * 4;
-  // tensor memory: accumulators | A operand (32 columns per chunk) | scale factors: per chunk
-  // 4 columns of weight scales (quarter q uses column q) + BN/32 columns of token scales,
-  // padded so every scale-factor address the MMA gets is a multiple of 4 columns
-  static constexpr int kTokSfCols = BN >= 32 ? BN / 32 : 1;
-  static constexpr int kSfColsPerChunk = 4 + cround(kTokSfCols, 4);
-  // narrow tiles alternate two accumulators along K so consecutive MMAs do not wait on
-  // each other's result; the epilogue adds them
-  static constexpr int kChains = BN <= 64 ? 2 : 1;
-  static constexpr int kAccCols = (kChains * BN) < 32 ? 32 : kChains * BN;
-  static constexpr int kPerStageCols = KS * (32 + kSfColsPerChunk);
-  static constexpr int kNumAcc = (2 * kAccCols + kStages * kPerStageCols <= 512) ? 2 : 1;
-  static constexpr int kACol0 = kNumAcc * kAccCols;
-  static constexpr int kSfCol0 = kACol0 + kStages * KS * 32;
-  static constexpr int kTmemCols = cpow2(kSfCol0 + kStages * KS * kSfColsPerChunk);
-  static constexpr int oCtl = kStages * kStageBytes;
+  static constexpr int SW = ring_depths(BM).sw;
+  static constexpr int SB = ring_depths(BM).sb;
+  static constexpr int ST = ring_depths(BM).st;
+  // token stage: BM rows x 128 B (128B-swizzled), then BM E8M0 words. The MMA reads 128 rows
+  // from the slot base; rows >= BM lie in the buffers that follow (their values are unused:
+  // they only reach accumulator lanes >= BM, which are never stored).
+  static constexpr int kTRowBytes = BM * 128;
+  static constexpr int kTStage = cround(BM * 128 + BM * 4, 1024);
+  static constexpr int kTTx = BM * 128 + BM * 4;
+  // weight stage: two 128-row halves x (8 KB codes, 64B-swizzled), then 2 x 1 KB scales
+  static constexpr int kWCodes = 16384;
+  static constexpr int kWStage = 16384 + 2048;
+  // B stage: 256 rows x 128 B E4M3 (128B-swizzled, K-major)
+  static constexpr int kBStage = 32768;
+  static constexpr int oT = 0;
+  static constexpr int oW = ST * kTStage;
+  static constexpr int oB = oW + SW * kWStage;
+  static constexpr int oSf = oB + SB * kBStage;  // SB x 256 E8M0 words staged for tensor memory
+  static constexpr int oCtl = oSf + SB * 1024;
   static constexpr int kCtlBytes = 2048;
   static constexpr int kSmemBytes = oCtl + kCtlBytes + 1024;  // + alignment slack
+  // tensor memory: accumulator (256 columns) | per B slot 12 scale columns: 4 token (A)
+  // columns (lane m reads column m / 32) then 8 weight (B) columns (row n at lane n % 32 of
+  // every lane quarter, column n / 32)
+  static constexpr int kSfCols = 12;
+  static constexpr int kSfCol0 = 256;
+  static constexpr int kTmemCols = 512;
   static constexpr int kTranscodeWarps = 16;
   static constexpr int kEpiWarps = 4;
-  static constexpr int kThreads = 32 * (2 + kEpiWarps + kTranscodeWarps);
+  static constexpr int kTProducerWarp = 2 + kEpiWarps + kTranscodeWarps;  // 22
+  static constexpr int kThreads = 32 * (kTProducerWarp + 1);
   static_assert(kSmemBytes <= 232448, "shared memory budget");
-  static_assert(kTmemCols <= 512, "tensor memory budget");
-  static_assert(kStages <= 8, "control block holds 8 stages");
-  static_assert(kSfCol0 % 4 == 0 && kSfColsPerChunk % 4 == 0 && kACol0 % 8 == 0,
-                "tensor-memory operand addresses stay 4-column aligned");
+  static_assert((ST - 1) * kTStage + 16384 <= oCtl, "token operand reads stay in the buffers");
+  static_assert(kSfCol0 + SB * kSfCols <= kTmemCols, "tensor memory budget");
+  static_assert(kSfCols % 4 == 0 && kSfCol0 % 4 == 0, "scale-factor addresses 4-column aligned");
+  static_assert(oW % 1024 == 0 && oB % 1024 == 0 && kTStage % 1024 == 0, "1 KB swizzle atoms");
+  static_assert(SW <= 8 && SB <= 4 && ST <= 4, "control block sizes");
 };
 
 struct GemmCtl {
-  uint64_t full[8], ready[8], empty[8], acc_full[2], acc_empty[2], drain;
+  uint64_t wfull[8], wempty[8], tfull[4], tempty[4], bready[4], bempty[4], sfready[4];
+  uint64_t acc_full, acc_empty, drain, fin_bar;
   uint32_t tmem_base;
+  uint32_t fin_job;  // 1: this CTA finishes the tile of its last segment
   uint32_t abort_flag;
   uint32_t bcast;
   TranscodeTables tab;
@@ -96,19 +112,22 @@ struct GemmCtl {
 
 struct GemmParams {
   void* out;                    // C, or the fp32 workspace planes (kOutPartial)
-  float* slots;                 // stream-K partial slots [grid][2][BN][128]
+  float* slots;                 // stream-K partial slots [grid][2][BM][256]
   uint32_t* counters;           // stream-K per-tile arrival counters (zero between calls)
   const __nv_bfloat16* bias;
   float tensor_scale;
   int M, N, K;
-  int n_tiles, m_tiles, nks;    // nks: pipeline stages (KS chunks) per tile
+  int n_tiles, m_tiles, nks;    // nks: 128-wide K chunks per tile
+  int n_half_tiles;             // N / 128 (128-row halves of the packed weights)
   int split_k;                  // 0 = stream-K, else explicit split
   int split_out;                // output mode of explicit split segments
   int out_dtype, epilogue;
+  int vec_out;                  // 1: C is 16-byte aligned (vector stores)
+  int weights_early;            // 1: B is not written by the grid this one may overlap
   uint32_t* err;
 };
 
-// One contiguous run of stages of one tile.
+// One contiguous run of chunks of one tile.
 struct Seg {
   int tile, k0, k1, z, slot;  // slot: -1 full tile, 0/1 stream-K partial slot
 };
@@ -116,7 +135,7 @@ struct Seg {
 // The work of CTA `c` of `G`: segment number `idx` (false when there is none). All indices
 // fit 32 bits (the host rejects larger problems).
 struct Schedule {
-  int U;        // units (tile, stage)
+  int U;        // units (tile, chunk)
   int q, r;     // stream-K: U = q*G + r
   int G, nks, tiles, split;
 
@@ -178,15 +197,48 @@ __device__ __forceinline__ void store_out(void* out, int64_t idx, float v, int d
   else reinterpret_cast<float*>(out)[idx] = v;
 }
 
-__device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
-                 "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
-
 __device__ __forceinline__ void named_barrier(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+
+// NV consecutive outputs (element index idx, a multiple of NV) in the output dtype; vector
+// stores (16 bytes, 8 for four 16-bit values) when C is 16-byte aligned.
+template <int NV>
+__device__ __forceinline__ void store_row(void* out, int64_t idx, const float (&v)[NV], int dtype,
+                                          int vec) {
+  if (!vec) {
+#pragma unroll
+    for (int j = 0; j < NV; ++j) store_out(out, idx + j, v[j], dtype);
+    return;
+  }
+  if (dtype == 2) {
+    float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + idx);
+#pragma unroll
+    for (int j = 0; j < NV / 4; ++j)
+      o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    return;
+  }
+  uint32_t w[NV / 2];
+#pragma unroll
+  for (int j = 0; j < NV / 2; ++j) {
+    if (dtype == 0) {
+      const __nv_bfloat162 b = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+      w[j] = *reinterpret_cast<const uint32_t*>(&b);
+    } else {
+      const __half2 b = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+      w[j] = *reinterpret_cast<const uint32_t*>(&b);
+    }
+  }
+  if constexpr (NV % 8 == 0) {
+    uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + idx);
+#pragma unroll
+    for (int j = 0; j < NV / 8; ++j)
+      o[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+  } else {
+    static_assert(NV == 4, "4, 8, 16 or 32 outputs");
+    *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(out) + idx) = make_uint2(w[0], w[1]);
+  }
 }
 
 // Eight E2M1 nibbles (one word) -> eight E4M3 bytes (two words) with the magnitude table
@@ -206,14 +258,91 @@ __device__ __forceinline__ uint32_t e8m0_of_pair(const TranscodeTables& t, uint3
   return static_cast<uint32_t>(max(e0, e1) + 111);
 }
 
-template <int BN, int KS>
-__global__ void __launch_bounds__(GemmCfg<BN, KS>::kThreads, 1)
+// Stream-K fix-up of one tile: C = sum of the contributors' fp32 partial slots, added in CTA
+// order (first..last), times the tensor scale, bias and activation. Worker `worker` of
+// `nworkers` takes float4 groups worker, worker + nworkers, ...; loads of up to four
+// contributors x two groups are in flight at once.
+template <int BM>
+__device__ __forceinline__ void streamk_reduce(const GemmParams& p, const Schedule& sch,
+                                               const Seg& sg, int first, int last, int worker,
+                                               int nworkers) {
+  const int mt = sg.tile / p.n_tiles, nt = sg.tile % p.n_tiles;
+  const int m0 = mt * BM, n0 = nt * kTileN;
+  const int mrows = min(BM, p.M - m0);
+  const int g4 = min(kTileN, p.N - n0) / 4;  // float4 groups per row
+  const int total = mrows * g4;
+  for (int g = worker; g < total; g += 2 * nworkers) {
+    float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+    int off[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int gi = g + u * nworkers;
+      const int rr = gi / g4;
+      off[u] = rr * kTileN + (gi - rr * g4) * 4;
+    }
+    for (int c = first; c <= last; c += 4) {
+      float4 v[4][2];
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const int ci = c + cc;
+        const int sl = (sch.u0(ci) / p.nks == sg.tile) ? 0 : 1;
+        const float* base = p.slots + (static_cast<int64_t>(ci) * 2 + sl) * (BM * kTileN);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          v[cc][u] = (ci <= last && g + u * nworkers < total)
+                         ? __ldcg(reinterpret_cast<const float4*>(base + off[u]))
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          acc[u].x += v[cc][u].x;
+          acc[u].y += v[cc][u].y;
+          acc[u].z += v[cc][u].z;
+          acc[u].w += v[cc][u].w;
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int gi = g + u * nworkers;
+      if (gi >= total) break;
+      const int rr = off[u] / kTileN, n = n0 + (off[u] - rr * kTileN);
+      float o[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        o[j] = apply_epilogue(o[j] * p.tensor_scale, p.epilogue, p.bias, n + j);
+      store_row<4>(p.out, static_cast<int64_t>(m0 + rr) * p.N + n, o, p.out_dtype, p.vec_out);
+    }
+  }
+}
+
+// Number of segments of CTA c and whether the last one is a stream-K partial.
+__device__ __forceinline__ int last_segment(const Schedule& sch, int c, Seg& last) {
+  int n = 0;
+  Seg sg;
+  while (sch.segment(c, n, sg)) {
+    last = sg;
+    ++n;
+  }
+  return n;
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
+template <int BM>
+__global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
     w4a6_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
                      const __grid_constant__ CUtensorMap tm_as,
                      const __grid_constant__ CUtensorMap tm_w,
                      const __grid_constant__ CUtensorMap tm_ws, const GemmParams p) {
-  using Cfg = GemmCfg<BN, KS>;
-  constexpr int S = Cfg::kStages;
+  using Cfg = GemmCfg<BM>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   GemmCtl& ctl = *reinterpret_cast<GemmCtl*>(smem + Cfg::oCtl);
@@ -226,98 +355,136 @@ __global__ void __launch_bounds__(GemmCfg<BN, KS>::kThreads, 1)
 
   if (tid == 0) {
     ctl.abort_flag = 0;
-    for (int s = 0; s < S; ++s) {
-      mbar_init(smem_u32(&ctl.full[s]), 1);
-      mbar_init(smem_u32(&ctl.ready[s]), Cfg::kTranscodeWarps);
-      mbar_init(smem_u32(&ctl.empty[s]), 1);
+    for (int s = 0; s < Cfg::SW; ++s) {
+      mbar_init(smem_u32(&ctl.wfull[s]), 1);
+      mbar_init(smem_u32(&ctl.wempty[s]), Cfg::kTranscodeWarps);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(&ctl.acc_full[b]), 1);
-      mbar_init(smem_u32(&ctl.acc_empty[b]), Cfg::kEpiWarps);
+    for (int s = 0; s < Cfg::ST; ++s) {
+      mbar_init(smem_u32(&ctl.tfull[s]), 1);
+      mbar_init(smem_u32(&ctl.tempty[s]), 1);
     }
+    for (int s = 0; s < Cfg::SB; ++s) {
+      mbar_init(smem_u32(&ctl.bready[s]), Cfg::kEpiWarps);
+      mbar_init(smem_u32(&ctl.bempty[s]), 1);
+      mbar_init(smem_u32(&ctl.sfready[s]), Cfg::kTranscodeWarps);
+    }
+    mbar_init(smem_u32(&ctl.acc_full), 1);
+    mbar_init(smem_u32(&ctl.acc_empty), Cfg::kEpiWarps);
     mbar_init(smem_u32(&ctl.drain), 1);
+    mbar_init(smem_u32(&ctl.fin_bar), 1);
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) {
-    prefetch_tmap(&tm_a);
-    prefetch_tmap(&tm_as);
-    prefetch_tmap(&tm_w);
-    prefetch_tmap(&tm_ws);
-  }
-  load_tables<true>(ctl.tab, tid, Cfg::kThreads);
-  if (warp == 1) {
-    tmem_alloc(smem_u32(&ctl.tmem_base), Cfg::kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
   __syncthreads();
-  tc_fence_after();
-  const uint32_t tbase = ctl.tmem_base;
+  // a grid launched after this one with programmatic serialisation may be scheduled now; it
+  // takes this SM only after this CTA exits, and waits for this grid before it reads A or
+  // touches C and the workspace
+  grid_dep_launch_dependents();
+  // The producers start at once. Everything that needs tensor memory or the transcode tables
+  // meets at named barrier 2 (warps 1..21) after warp 1 allocated and the transcode warps
+  // copied the tables.
+  uint32_t tbase = 0;
+  if (warp >= 1 && warp < Cfg::kTProducerWarp) {
+    if (warp == 1) {
+      tmem_alloc(smem_u32(&ctl.tmem_base), Cfg::kTmemCols);
+      tmem_relinquish();
+    } else if (warp >= 2 + Cfg::kEpiWarps) {
+      load_tables<true>(ctl.tab, tid - 32 * (2 + Cfg::kEpiWarps), 32 * Cfg::kTranscodeWarps);
+    }
+    tc_fence_before();
+    named_barrier(2, 32 * (Cfg::kTProducerWarp - 1));
+    tc_fence_after();
+    tbase = ctl.tmem_base;
+  }
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ producer
+    // ------------------------------------------------------------------ weight producer
     if (lane == 0) {
-      int i = 0;
+      prefetch_tmap(&tm_w);
+      prefetch_tmap(&tm_ws);
+      if (!p.weights_early) grid_dep_wait();
+      RingPos<Cfg::SW> w;
       Seg sg;
       for (int idx = 0; sch.segment(cta, idx, sg) && !*abort_flag; ++idx) {
-        const int mt = sg.tile / p.n_tiles, nt = sg.tile % p.n_tiles;
-        for (int k = sg.k0; k < sg.k1; ++k, ++i) {
-          const int s = i % S;
-          const uint32_t ph = (i / S) & 1;
-          if (!mbar_wait(smem_u32(&ctl.empty[s]), ph ^ 1u, p.err, kErrWaitEmpty, abort_flag)) break;
-          uint8_t* st = smem + s * Cfg::kStageBytes;
-          const uint32_t fb = smem_u32(&ctl.full[s]);
-          const int kt = k * KS;
-          const int32_t chunk = nt * (p.nks * KS) + kt;
-          mbar_arrive_expect_tx(fb, Cfg::kTxBytes);
-          tma_load_2d(smem_u32(st + Cfg::oWCode), &tm_w, 0, chunk * 128, fb);
-          tma_load_2d(smem_u32(st + Cfg::oWScale), &tm_ws, 0, chunk, fb);
-          tma_load_3d(smem_u32(st + Cfg::oTok), &tm_a, 0, mt * BN, kt, fb);
-          tma_load_2d(smem_u32(st + Cfg::oTokScale), &tm_as, mt * BN, kt, fb);
+        const int nt = sg.tile % p.n_tiles;
+        // the second 128-row half is missing in the last tile when N / 128 is odd
+        const bool two = 2 * nt + 1 < p.n_half_tiles;
+        const uint32_t tx = two ? Cfg::kWStage : Cfg::kWStage / 2;
+        int row0 = (2 * nt) * p.nks + sg.k0;  // (half tile, chunk) row of the packed weights
+        for (int k = sg.k0; k < sg.k1; ++k, ++row0) {
+          if (!mbar_wait(smem_u32(&ctl.wempty[w.slot]), w.phase ^ 1u, p.err, kErrWaitEmpty,
+                         abort_flag))
+            break;
+          uint8_t* st = smem + Cfg::oW + w.slot * Cfg::kWStage;
+          const uint32_t fb = smem_u32(&ctl.wfull[w.slot]);
+          mbar_arrive_expect_tx(fb, tx);
+          tma_load_2d(smem_u32(st), &tm_w, 0, row0 * 128, fb);
+          tma_load_2d(smem_u32(st + Cfg::kWCodes), &tm_ws, 0, row0, fb);
+          if (two) {
+            tma_load_2d(smem_u32(st + 8192), &tm_w, 0, (row0 + p.nks) * 128, fb);
+            tma_load_2d(smem_u32(st + Cfg::kWCodes + 1024), &tm_ws, 0, row0 + p.nks, fb);
+          }
+          w.next();
+        }
+      }
+    }
+  } else if (warp == Cfg::kTProducerWarp) {
+    // ------------------------------------------------------------------ token producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_a);
+      prefetch_tmap(&tm_as);
+      grid_dep_wait();  // A may be written by the previous grid
+      RingPos<Cfg::ST> t;
+      Seg sg;
+      for (int idx = 0; sch.segment(cta, idx, sg) && !*abort_flag; ++idx) {
+        const int mt = sg.tile / p.n_tiles;
+        for (int k = sg.k0; k < sg.k1; ++k) {
+          if (!mbar_wait(smem_u32(&ctl.tempty[t.slot]), t.phase ^ 1u, p.err, kErrWaitEmpty,
+                         abort_flag))
+            break;
+          uint8_t* st = smem + Cfg::oT + t.slot * Cfg::kTStage;
+          const uint32_t fb = smem_u32(&ctl.tfull[t.slot]);
+          mbar_arrive_expect_tx(fb, Cfg::kTTx);
+          tma_load_3d(smem_u32(st), &tm_a, 0, mt * BM, k, fb);
+          tma_load_2d(smem_u32(st + Cfg::kTRowBytes), &tm_as, mt * BM, k, fb);
+          t.next();
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      int i = 0;
+      RingPos<Cfg::SB> b;
+      RingPos<Cfg::ST> t;
       Seg sg;
       for (int idx = 0; sch.segment(cta, idx, sg); ++idx) {
-        const int buf = Cfg::kNumAcc == 2 ? (idx & 1) : 0;
-        const uint32_t use = Cfg::kNumAcc == 2 ? (idx >> 1) : idx;
-        if (!mbar_wait(smem_u32(&ctl.acc_empty[buf]), (use & 1) ^ 1u, p.err, kErrWaitAccum,
-                       abort_flag))
+        if (!mbar_wait(smem_u32(&ctl.acc_empty), (idx & 1) ^ 1u, p.err, kErrWaitAccum,
+                            abort_flag))
           break;
         tc_fence_after();
-        const uint32_t tD = tbase + buf * Cfg::kAccCols;
         bool ok = true;
-        for (int k = sg.k0; k < sg.k1; ++k, ++i) {
-          const int s = i % S;
-          const uint32_t ph = (i / S) & 1;
-          if (!mbar_wait(smem_u32(&ctl.ready[s]), ph, p.err, kErrWaitOperand, abort_flag)) {
+        for (int k = sg.k0; k < sg.k1; ++k) {
+          if (!mbar_wait(smem_u32(&ctl.bready[b.slot]), b.phase, p.err, kErrWaitOperand,
+                         abort_flag) ||
+              !mbar_wait(smem_u32(&ctl.tfull[t.slot]), t.phase, p.err, kErrWaitTma, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t tok = smem_u32(smem + s * Cfg::kStageBytes + Cfg::oTok);
+          const uint32_t a_addr = smem_u32(smem + Cfg::oT + t.slot * Cfg::kTStage);
+          const uint32_t b_addr = smem_u32(smem + Cfg::oB + b.slot * Cfg::kBStage);
+          const uint32_t sfa = tbase + Cfg::kSfCol0 + b.slot * Cfg::kSfCols;
 #pragma unroll
-          for (int h = 0; h < KS; ++h) {
-            const uint32_t tA = tbase + Cfg::kACol0 + (s * KS + h) * 32;
-            const uint32_t tSfW = tbase + Cfg::kSfCol0 + (s * KS + h) * Cfg::kSfColsPerChunk;
-            const uint32_t tSfA = tSfW + 4;
-            const uint32_t ab = tok + h * BN * 128;
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint32_t idesc = idesc_mxf8f6f4(128, BN, kFmtE4M3, kFmtE2M3, kk, kk);
-              const int chain = kk % Cfg::kChains;
-              const bool first = (k == sg.k0 && h == 0 && kk < Cfg::kChains);
-              mma_mxf8f6f4_ts(tD + chain * BN, tA + kk * 8, sdesc_sw128(ab + kk * 32), idesc,
-                              tSfW, tSfA, first ? 0u : 1u);
-            }
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t idesc = idesc_mxf8f6f4(128, kTileN, kFmtE2M3, kFmtE4M3, kk, kk);
+            mma_mxf8f6f4_ss(tbase, sdesc_sw128(a_addr + kk * 32), sdesc_sw128(b_addr + kk * 32),
+                            idesc, sfa, sfa + 4, (k == sg.k0 && kk == 0) ? 0u : 1u);
           }
-          tc_commit(smem_u32(&ctl.empty[s]));
+          tc_commit(smem_u32(&ctl.bempty[b.slot]));
+          tc_commit(smem_u32(&ctl.tempty[t.slot]));
+          b.next();
+          t.next();
         }
-        tc_commit(smem_u32(&ctl.acc_full[buf]));
+        tc_commit(smem_u32(&ctl.acc_full));
         if (!ok) break;
       }
       // arrives once every tcgen05 operation this thread issued has completed
@@ -325,141 +492,167 @@ __global__ void __launch_bounds__(GemmCfg<BN, KS>::kThreads, 1)
     }
   } else if (warp >= 2 + Cfg::kEpiWarps) {
     // ------------------------------------------------------------------ transcode
-    // Software-pipelined by one stage: the tensor-memory stores of stage i drain while stage
-    // i+1 is loaded and converted; only then does the warp wait for them and signal ready(i).
-    // (Stage i+1's data never depends on ready(i): the producer is S >= 2 stages ahead.)
-    const int tw = warp - 2 - Cfg::kEpiWarps;   // 0..15
-    const int quarter = warp & 3;               // TMEM lane quarter this warp may access
-    const int j = tw >> 2;                      // K block (32 elements) of each chunk
-    const int row = quarter * 32 + lane;
-    const uint32_t lane_base = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
-    int i = 0, prev = -1;
+    const int tw = warp - 2 - Cfg::kEpiWarps;  // 0..15
+    const int row = tw * 16 + (lane & 15);     // weight row of the tile
+    const int hk = lane >> 4;                  // K blocks 2hk, 2hk + 1 of each chunk
+    const int rr = row & 127;
+    const int half_off = (row >> 7) * 8192;
+    // raw codes: 64B-swizzled 128-row halves, 16-byte chunk c of row rr at
+    // rr*64 + ((c ^ ((rr >> 1) & 3)) << 4); chunk c holds K block c
+    const int code_off0 = half_off + rr * 64 + (((2 * hk) ^ ((rr >> 1) & 3)) << 4);
+    const int code_off1 = half_off + rr * 64 + (((2 * hk + 1) ^ ((rr >> 1) & 3)) << 4);
+    const int scale_off = Cfg::kWCodes + (row >> 7) * 1024 + rr * 8 + hk * 4;
+    // B operand: 128B-swizzled K-major, 16-byte chunk cc of row r at
+    // (r >> 3)*1024 + (r & 7)*128 + ((cc ^ (r & 7)) << 4); block b covers chunks 2b, 2b + 1
+    const int b_row = (row >> 3) * 1024 + (row & 7) * 128;
+    const int r7 = row & 7;
+    RingPos<Cfg::SW> w;
+    RingPos<Cfg::SB> b;
     Seg sg;
     for (int idx = 0; sch.segment(cta, idx, sg) && !*abort_flag; ++idx) {
-      for (int k = sg.k0; k < sg.k1; ++k, ++i) {
-        const int s = i % S;
-        const uint32_t ph = (i / S) & 1;
-        if (!mbar_wait(smem_u32(&ctl.full[s]), ph, p.err, kErrWaitTma, abort_flag)) break;
-        const uint8_t* st = smem + s * Cfg::kStageBytes;
-        uint32_t v[KS][8];
-        uint32_t sfw_word[KS];
-        uint32_t tok[KS][Cfg::kTokSfCols];
-#pragma unroll
-        for (int h = 0; h < KS; ++h) {
-          // 64B-swizzled codes: 16-byte chunk c of row r at r*64 + (c ^ ((r >> 1) & 3)) * 16
-          const uint4 q = *reinterpret_cast<const uint4*>(
-              st + Cfg::oWCode + h * 8192 + row * 64 + ((j ^ ((row >> 1) & 3)) << 4));
-          const uint8_t* srow = st + Cfg::oWScale + h * 1024 + row * 8;
-          const uint32_t sc = *reinterpret_cast<const uint16_t*>(srow + j * 2);
+      for (int k = sg.k0; k < sg.k1; ++k) {
+        if (!mbar_wait(smem_u32(&ctl.wfull[w.slot]), w.phase, p.err, kErrWaitTma, abort_flag))
+          break;
+        const uint8_t* st = smem + Cfg::oW + w.slot * Cfg::kWStage;
+        const uint4 q0 = *reinterpret_cast<const uint4*>(st + code_off0);
+        const uint4 q1 = *reinterpret_cast<const uint4*>(st + code_off1);
+        const uint32_t sc = *reinterpret_cast<const uint32_t*>(st + scale_off);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&ctl.wempty[w.slot]));
+        w.next();
+        uint32_t v0[8], v1[8];
+        uint32_t e0, e1;
+        {
           uint2 T0, T1;
-          uint32_t e8;
-          scale_pair(ctl.tab, sc & 0xFFu, sc >> 8, T0, T1, e8);
-          nib8_to_e4m3(q.x, T0, v[h][0], v[h][1]);
-          nib8_to_e4m3(q.y, T0, v[h][2], v[h][3]);
-          nib8_to_e4m3(q.z, T1, v[h][4], v[h][5]);
-          nib8_to_e4m3(q.w, T1, v[h][6], v[h][7]);
-          if (j == 0) {
-            // weight scales of this row's four K blocks, one word for column sfw + quarter
-            const uint2 all = *reinterpret_cast<const uint2*>(srow);
-            sfw_word[h] = e8m0_of_pair(ctl.tab, all.x & 0xFFu, (all.x >> 8) & 0xFFu) |
-                          (e8m0_of_pair(ctl.tab, (all.x >> 16) & 0xFFu, all.x >> 24) << 8) |
-                          (e8m0_of_pair(ctl.tab, all.y & 0xFFu, (all.y >> 8) & 0xFFu) << 16) |
-                          (e8m0_of_pair(ctl.tab, (all.y >> 16) & 0xFFu, all.y >> 24) << 24);
-          } else if (j == 1) {
-            // token scales: token n = lane + 32c at column c, in every lane quarter
-            const uint32_t* raw = reinterpret_cast<const uint32_t*>(st + Cfg::oTokScale) + h * BN;
-#pragma unroll
-            for (int c = 0; c < Cfg::kTokSfCols; ++c)
-              tok[h][c] = (lane + 32 * c < BN) ? raw[lane + 32 * c] : 0u;
-          }
+          scale_pair(ctl.tab, sc & 0xFFu, (sc >> 8) & 0xFFu, T0, T1, e0);
+          nib8_to_e4m3(q0.x, T0, v0[0], v0[1]);
+          nib8_to_e4m3(q0.y, T0, v0[2], v0[3]);
+          nib8_to_e4m3(q0.z, T1, v0[4], v0[5]);
+          nib8_to_e4m3(q0.w, T1, v0[6], v0[7]);
         }
-        if (prev >= 0) {
-          tmem_st_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&ctl.ready[prev]));
+        {
+          uint2 T0, T1;
+          scale_pair(ctl.tab, (sc >> 16) & 0xFFu, sc >> 24, T0, T1, e1);
+          nib8_to_e4m3(q1.x, T0, v1[0], v1[1]);
+          nib8_to_e4m3(q1.y, T0, v1[2], v1[3]);
+          nib8_to_e4m3(q1.z, T1, v1[4], v1[5]);
+          nib8_to_e4m3(q1.w, T1, v1[6], v1[7]);
         }
-#pragma unroll
-        for (int h = 0; h < KS; ++h) {
-          tmem_st_x8(lane_base + Cfg::kACol0 + (s * KS + h) * 32 + j * 8, v[h]);
-          const uint32_t sfw = Cfg::kSfCol0 + (s * KS + h) * Cfg::kSfColsPerChunk;
-          if (j == 0) {
-            tmem_st_x1(lane_base + sfw + quarter, sfw_word[h]);
-          } else if (j == 1) {
-            if constexpr (Cfg::kTokSfCols == 1) {
-              tmem_st_x1(lane_base + sfw + 4, tok[h][0]);
-            } else if constexpr (Cfg::kTokSfCols == 2) {
-              tmem_st_x2(lane_base + sfw + 4, tok[h][0], tok[h][1]);
-            } else if constexpr (Cfg::kTokSfCols == 4) {
-              tmem_st_x4(lane_base + sfw + 4, tok[h][0], tok[h][1], tok[h][2], tok[h][3]);
-            } else {
-              uint32_t t8[8];
-#pragma unroll
-              for (int c = 0; c < 8; ++c) t8[c] = tok[h][c % Cfg::kTokSfCols];
-              tmem_st_x8(lane_base + sfw + 4, t8);
-            }
-          }
-        }
-        prev = s;
+        // E8M0 word of this row: blocks 0..3 in bytes 0..3 (lanes l and l ^ 16 share the row)
+        const uint32_t mine = e0 | (e1 << 8);
+        const uint32_t other = __shfl_xor_sync(0xFFFFFFFFu, mine, 16);
+        const uint32_t sfw = hk == 0 ? (mine | (other << 16)) : (other | (mine << 16));
+        if (!mbar_wait(smem_u32(&ctl.bempty[b.slot]), b.phase ^ 1u, p.err, kErrWaitMma,
+                       abort_flag))
+          break;
+        const uint32_t bt = smem_u32(smem + Cfg::oB + b.slot * Cfg::kBStage) + b_row;
+        const int c0 = 4 * hk;  // first 16-byte chunk of block 2hk
+        st_shared_v4(bt + (((c0 + 0) ^ r7) << 4), v0[0], v0[1], v0[2], v0[3]);
+        st_shared_v4(bt + (((c0 + 1) ^ r7) << 4), v0[4], v0[5], v0[6], v0[7]);
+        st_shared_v4(bt + (((c0 + 2) ^ r7) << 4), v1[0], v1[1], v1[2], v1[3]);
+        st_shared_v4(bt + (((c0 + 3) ^ r7) << 4), v1[4], v1[5], v1[6], v1[7]);
+        uint32_t* sf_stage = reinterpret_cast<uint32_t*>(smem + Cfg::oSf + b.slot * 1024);
+        if (hk == 0) sf_stage[row] = sfw;
+        fence_proxy_async_smem();  // the tensor core reads the B tile through the async proxy
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&ctl.sfready[b.slot]));
+        b.next();
       }
     }
-    if (prev >= 0) {
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&ctl.ready[prev]));
+    // the fix-up of the tile of this CTA's last segment, when this CTA finishes it, is shared
+    // with the epilogue warps (workers 128.. of 640)
+    Seg lastseg;
+    if (p.split_k == 0 && last_segment(sch, cta, lastseg) > 0 && lastseg.slot >= 0 &&
+        !*abort_flag &&
+        mbar_wait(smem_u32(&ctl.fin_bar), 0, p.err, kErrWaitAccum, abort_flag) &&
+        ctl.fin_job != 0) {
+      __threadfence();
+      const int first = sch.cta_of(lastseg.tile * p.nks);
+      const int last = sch.cta_of((lastseg.tile + 1) * p.nks - 1);
+      streamk_reduce<BM>(p, sch, lastseg, first, last, 32 * Cfg::kEpiWarps + 32 * tw + lane,
+                         32 * (Cfg::kEpiWarps + Cfg::kTranscodeWarps));
     }
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..5)
-    // accumulator columns per tensor-memory load
-    constexpr int kB = (BN < 32 || Cfg::kChains == 2) ? 16 : 32;
     const int quarter = warp & 3;
     const int ep_tid = tid - 64;  // 0..127
+    const int mrow = quarter * 32 + lane;  // token row of the tile (accumulator lane)
+    constexpr int kEB = 16;                // accumulator columns per tensor-memory load
+    grid_dep_wait();  // C, bias and the workspace belong to the previous grid until it ends
+    const uint32_t taddr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
+    Seg lastseg;
+    const int nseg = last_segment(sch, cta, lastseg);
+    RingPos<Cfg::SB> b;
+    RingPos<Cfg::ST> t;
     Seg sg;
-    for (int idx = 0; sch.segment(cta, idx, sg); ++idx) {
-      const int buf = Cfg::kNumAcc == 2 ? (idx & 1) : 0;
-      const uint32_t use = Cfg::kNumAcc == 2 ? (idx >> 1) : idx;
-      if (!mbar_wait(smem_u32(&ctl.acc_full[buf]), use & 1, p.err, kErrWaitAccum, abort_flag))
+    for (int idx = 0; sch.segment(cta, idx, sg) && !*abort_flag; ++idx) {
+      // Scale factors of each chunk of this segment into tensor memory, in this warp's lane
+      // quarter: token m = 32 quarter + lane at column quarter, weight row 32c + lane at
+      // column 4 + c (every quarter holds a copy of the weight scales). Staged by the
+      // transcode warps (sfready); the MMA waits for all four quarters (bready).
+      bool ok = true;
+      for (int k = sg.k0; k < sg.k1; ++k) {
+        if (!mbar_wait(smem_u32(&ctl.sfready[b.slot]), b.phase, p.err, kErrWaitOperand,
+                       abort_flag) ||
+            !mbar_wait(smem_u32(&ctl.tfull[t.slot]), t.phase, p.err, kErrWaitTma, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint32_t* tok = reinterpret_cast<const uint32_t*>(
+            smem + Cfg::oT + t.slot * Cfg::kTStage + Cfg::kTRowBytes);
+        const uint32_t tokw = mrow < BM ? tok[mrow] : 0u;
+        const uint32_t* sf_stage = reinterpret_cast<const uint32_t*>(smem + Cfg::oSf + b.slot * 1024);
+        uint32_t wv[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) wv[c] = sf_stage[32 * c + lane];
+        const uint32_t col = taddr + Cfg::kSfCol0 + b.slot * Cfg::kSfCols;
+        tmem_st_x1(col + quarter, tokw);
+        tmem_st_x8(col + 4, wv);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&ctl.bready[b.slot]));
+        b.next();
+        t.next();
+      }
+      if (!ok) break;
+      if (!mbar_wait(smem_u32(&ctl.acc_full), idx & 1, p.err, kErrWaitAccum, abort_flag))
         break;
       tc_fence_after();
       const int mt = sg.tile / p.n_tiles, nt = sg.tile % p.n_tiles;
-      const int n = nt * 128 + quarter * 32 + lane;
-      const int m0 = mt * BN;
-      const int mcols = min(BN, p.M - m0);  // valid token columns of this tile
-      const uint32_t taddr =
-          tbase + buf * Cfg::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16);
-      const int row = quarter * 32 + lane;
-      // accumulator columns [c0, c0 + kB) of this thread's row, chains added
-      auto load_acc = [&](int c0, float (&acc)[kB]) {
-        uint32_t r[kB];
-        if constexpr (kB == 16) tmem_ld_x16(taddr + c0, r); else tmem_ld_x32(taddr + c0, r);
-        if constexpr (Cfg::kChains == 2) {
-          uint32_t r2[kB];
-          if constexpr (kB == 16) tmem_ld_x16(taddr + BN + c0, r2);
-          else tmem_ld_x32(taddr + BN + c0, r2);
-          tmem_ld_wait();
-#pragma unroll
-          for (int jj = 0; jj < kB; ++jj) acc[jj] = __uint_as_float(r[jj]) + __uint_as_float(r2[jj]);
-        } else {
-          tmem_ld_wait();
-#pragma unroll
-          for (int jj = 0; jj < kB; ++jj) acc[jj] = __uint_as_float(r[jj]);
-        }
-      };
-      bool finish = false;
-      int first = 0, last = -1;
+      const int m0 = mt * BM, n0 = nt * kTileN;
+      const int mrows = min(BM, p.M - m0);       // valid token rows of this tile
+      const int ncols = min(kTileN, p.N - n0);   // valid weight rows (multiple of 128)
+      const bool warp_rows = quarter * 32 < mrows;
+      const bool row_ok = mrow < mrows;
+      const int m = m0 + mrow;
       if (sg.slot >= 0) {
-        // stream-K partial: store the slot, then count arrivals for this tile
-        float* slot = p.slots + (static_cast<int64_t>(cta) * 2 + sg.slot) * (BN * 128);
-        for (int c0 = 0; c0 < mcols; c0 += kB) {
-          float acc[kB];
-          load_acc(c0, acc);
+        // stream-K partial: store it in this CTA's slot, free the accumulator, count the
+        // arrivals for this tile; the last contributor sums all slots in CTA order (so the
+        // result does not depend on which CTA arrived last), all 128 threads sharing the work
+        float* slot = p.slots + (static_cast<int64_t>(cta) * 2 + sg.slot) * (BM * kTileN);
+        if (warp_rows) {
+          for (int c0 = 0; c0 < ncols; c0 += kEB) {
+            uint32_t r[kEB];
+            __syncwarp();
+            tmem_ld_x16(taddr + c0, r);
+            tmem_ld_wait();
+            if (row_ok) {
+              float4* dst = reinterpret_cast<float4*>(slot + mrow * kTileN + c0);
 #pragma unroll
-          for (int jj = 0; jj < kB; ++jj) __stcg(slot + (c0 + jj) * 128 + row, acc[jj]);
+              for (int j = 0; j < kEB / 4; ++j)
+                __stcg(dst + j, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                            __uint_as_float(r[4 * j + 2]),
+                                            __uint_as_float(r[4 * j + 3])));
+            }
+          }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&ctl.acc_empty));
         __threadfence();
-        first = sch.cta_of(sg.tile * p.nks);
-        last = sch.cta_of((sg.tile + 1) * p.nks - 1);
+        const int first = sch.cta_of(sg.tile * p.nks);
+        const int last = sch.cta_of((sg.tile + 1) * p.nks - 1);
         named_barrier(1, 32 * Cfg::kEpiWarps);
         if (ep_tid == 0) {
           const uint32_t old = atomicAdd(p.counters + sg.tile, 1u);
@@ -468,69 +661,69 @@ __global__ void __launch_bounds__(GemmCfg<BN, KS>::kThreads, 1)
           ctl.bcast = fin ? 1u : 0u;
         }
         named_barrier(1, 32 * Cfg::kEpiWarps);
-        finish = ctl.bcast != 0;
+        const bool finish = ctl.bcast != 0;
         named_barrier(1, 32 * Cfg::kEpiWarps);
-        if (finish) __threadfence();
+        const bool helped = idx == nseg - 1;  // the transcode warps are idle by then
+        if (helped && ep_tid == 0) {
+          ctl.fin_job = finish ? 1u : 0u;
+          __threadfence();
+          mbar_arrive(smem_u32(&ctl.fin_bar));
+        }
+        if (finish) {
+          __threadfence();
+          streamk_reduce<BM>(p, sch, sg, first, last, ep_tid,
+                             helped ? 32 * (Cfg::kEpiWarps + Cfg::kTranscodeWarps)
+                                    : 32 * Cfg::kEpiWarps);
+        }
+        continue;
       }
-      if (sg.slot < 0 || finish) {
-        for (int c0 = 0; c0 < mcols; c0 += kB) {
-          float acc[kB];
-          load_acc(c0, acc);   // this CTA's own part straight from tensor memory
-          if (finish) {
-            // add the contributors in CTA order (own part in its place): the result does not
-            // depend on which CTA happened to arrive last
-            float own[kB];
+      if (warp_rows) {
+        for (int c0 = 0; c0 < ncols; c0 += kEB) {
+          uint32_t r[kEB];
+          __syncwarp();
+          tmem_ld_x16(taddr + c0, r);
+          tmem_ld_wait();
+          if (!row_ok) continue;  // the warp meets again at the next __syncwarp
+          float acc[kEB];
 #pragma unroll
-            for (int jj = 0; jj < kB; ++jj) {
-              own[jj] = acc[jj];
-              acc[jj] = 0.0f;
-            }
-            for (int c = first; c <= last; ++c) {
-              if (c == cta) {
+          for (int j = 0; j < kEB; ++j) acc[j] = __uint_as_float(r[j]);
+          const int n = n0 + c0;
+          const int64_t rowbase = static_cast<int64_t>(m) * p.N + n;
+          if (p.split_k <= 1 && p.split_out == kOutAtomic) {
+            float* o = reinterpret_cast<float*>(p.out) + rowbase;
 #pragma unroll
-                for (int jj = 0; jj < kB; ++jj) acc[jj] += own[jj];
-                continue;
-              }
-              const int sl = (sch.u0(c) / p.nks == sg.tile) ? 0 : 1;
-              const float* slot = p.slots + (static_cast<int64_t>(c) * 2 + sl) * (BN * 128);
+            for (int j = 0; j < kEB; ++j) atomicAdd(o + j, acc[j] * p.tensor_scale);
+          } else if (p.split_k <= 1) {
 #pragma unroll
-              for (int jj = 0; jj < kB; ++jj) acc[jj] += __ldcg(slot + (c0 + jj) * 128 + row);
-            }
-          }
+            for (int j = 0; j < kEB; ++j)
+              acc[j] = apply_epilogue(acc[j] * p.tensor_scale, p.epilogue, p.bias, n + j);
+            store_row<kEB>(p.out, rowbase, acc, p.out_dtype, p.vec_out);
+          } else if (p.split_out == kOutPartial) {
+            float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) +
+                                                  static_cast<int64_t>(sg.z) * p.M * p.N + rowbase);
 #pragma unroll
-          for (int jj = 0; jj < kB; ++jj) {
-            const int m = m0 + c0 + jj;
-            if (c0 + jj < mcols) {
-              const float a = acc[jj];
-              if (p.split_k == 0 || p.split_k == 1) {
-                if (p.split_out == kOutAtomic) {
-                  atomicAdd(reinterpret_cast<float*>(p.out) + static_cast<int64_t>(m) * p.N + n,
-                            a * p.tensor_scale);
-                } else {
-                  store_out(p.out, static_cast<int64_t>(m) * p.N + n,
-                            apply_epilogue(a * p.tensor_scale, p.epilogue, p.bias, n),
-                            p.out_dtype);
-                }
-              } else if (p.split_out == kOutPartial) {
-                reinterpret_cast<float*>(p.out)[(static_cast<int64_t>(sg.z) * p.M + m) * p.N + n] = a;
-              } else if (p.split_out == kOutPlane) {
-                store_out(p.out, (static_cast<int64_t>(sg.z) * p.M + m) * p.N + n,
-                          a * p.tensor_scale, p.out_dtype);
-              } else {
-                atomicAdd(reinterpret_cast<float*>(p.out) + static_cast<int64_t>(m) * p.N + n,
-                          a * p.tensor_scale);
-              }
-            }
+            for (int j = 0; j < kEB / 4; ++j)
+              o[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+          } else if (p.split_out == kOutPlane) {
+#pragma unroll
+            for (int j = 0; j < kEB; ++j) acc[j] *= p.tensor_scale;
+            store_row<kEB>(p.out, static_cast<int64_t>(sg.z) * p.M * p.N + rowbase, acc,
+                           p.out_dtype, p.vec_out);
+          } else {
+            float* o = reinterpret_cast<float*>(p.out) + rowbase;
+#pragma unroll
+            for (int j = 0; j < kEB; ++j) atomicAdd(o + j, acc[j] * p.tensor_scale);
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&ctl.acc_empty[buf]));
+      if (lane == 0) mbar_arrive(smem_u32(&ctl.acc_empty));
     }
   }
 
   // ------------------------------------------------------------------ teardown
+  __syncwarp();  // lanes that skipped a role's single-thread loop meet their lane 0 here
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -48,6 +48,16 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
+// Programmatic dependent launch (griddepcontrol, sm_90+). wait: block until the grids this
+// one depends on have completed and their memory is visible (returns at once when the
+// launch had no programmatic dependency). launch_dependents: allow the next grid on the
+// stream, if launched with programmatic serialisation, to be scheduled.
+__device__ __forceinline__ void grid_dep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -84,33 +94,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_
         if (abort_flag) *abort_flag = 1u;
         return false;
       }
-    }
-  }
-}
-
-// Same, for waits expected to last long (a whole accumulation): try_wait is given a
-// suspend-time hint so the waiting warp sleeps in hardware instead of spinning.
-__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000000;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_wait_long(uint32_t bar, uint32_t parity, uint32_t* err,
-                                               uint32_t code, volatile uint32_t* abort_flag) {
-  const long long t0 = clock64();
-  while (true) {
-    if (mbar_try_wait_sleep(bar, parity)) return true;
-    if (abort_flag != nullptr && *abort_flag) return false;
-    if (static_cast<unsigned long long>(clock64() - t0) > kWaitLimitCycles) {
-      if (err) atomicOr(err, code);
-      if (abort_flag) *abort_flag = 1u;
-      return false;
     }
   }
 }

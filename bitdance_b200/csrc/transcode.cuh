@@ -74,23 +74,40 @@ __host__ __device__ constexpr PermTable make_perm(bool e4m3) {
   return t;
 }
 
-__constant__ ScaleInfoTable c_scale_info = make_scale_info();
-__constant__ PermTable c_perm_e2m3 = make_perm(false);
-__constant__ PermTable c_perm_e4m3 = make_perm(true);
-
 // Shared-memory copies of the tables (filled by every kernel that transcodes).
-struct TranscodeTables {
-  uint2 perm[64];       // (mb*8 + d) -> 8 magnitude bytes
+struct alignas(16) TranscodeTables {
+  uint2 perm[64];       // (d*8 + mb) -> 8 magnitude bytes
   uint8_t info[128];    // scale byte class
 };
+static_assert(sizeof(TranscodeTables) == 640, "tables copied as 40 16-byte words");
+
+__host__ __device__ constexpr TranscodeTables make_tables(bool e4m3) {
+  TranscodeTables t{};
+  const PermTable p = make_perm(e4m3);
+  // stored d-major: a warp's lookups are mostly d in {0, 1}, whose 16 rows then fall in 16
+  // different bank pairs
+  for (int mb = 0; mb < 8; ++mb)
+    for (int d = 0; d < 8; ++d) {
+      const int i = mb * 8 + d;
+      t.perm[d * 8 + mb] = uint2{p.w[2 * i], p.w[2 * i + 1]};
+    }
+  const ScaleInfoTable s = make_scale_info();
+  for (int i = 0; i < 128; ++i) t.info[i] = s.v[i];
+  return t;
+}
+
+// The tables live in global memory and are copied with one coalesced 16-byte load per
+// thread: per-thread-divergent reads of __constant__ data serialise within a warp, which at
+// kernel start (cold constant cache) cost microseconds.
+__device__ const TranscodeTables g_tables_e2m3 = make_tables(false);
+__device__ const TranscodeTables g_tables_e4m3 = make_tables(true);
 
 template <bool kE4M3>
 __device__ __forceinline__ void load_tables(TranscodeTables& t, int tid, int nthreads) {
-  for (int i = tid; i < 64; i += nthreads) {
-    const PermTable& p = kE4M3 ? c_perm_e4m3 : c_perm_e2m3;
-    t.perm[i] = make_uint2(p.w[2 * i], p.w[2 * i + 1]);
-  }
-  for (int i = tid; i < 128; i += nthreads) t.info[i] = c_scale_info.v[i];
+  const uint4* src = reinterpret_cast<const uint4*>(kE4M3 ? &g_tables_e4m3 : &g_tables_e2m3);
+  uint4* dst = reinterpret_cast<uint4*>(&t);
+  for (int i = tid; i < static_cast<int>(sizeof(TranscodeTables) / 16); i += nthreads)
+    dst[i] = __ldg(src + i);
 }
 
 // Scale pair -> (table rows for each half, E8M0 byte).
@@ -100,8 +117,8 @@ __device__ __forceinline__ void scale_pair(const TranscodeTables& t, uint32_t s0
   const int e0 = static_cast<int>(i0 >> 3), e1 = static_cast<int>(i1 >> 3);
   const int emax = max(e0, e1);
   const int d0 = min(emax - e0, 7), d1 = min(emax - e1, 7);
-  T0 = t.perm[(i0 & 7u) * 8u + d0];
-  T1 = t.perm[(i1 & 7u) * 8u + d1];
+  T0 = t.perm[static_cast<uint32_t>(d0) * 8u + (i0 & 7u)];
+  T1 = t.perm[static_cast<uint32_t>(d1) * 8u + (i1 & 7u)];
   e8m0 = static_cast<uint32_t>(emax + 111);  // (e + 16) - 16 + 127
 }
 

@@ -130,6 +130,24 @@ int bd_w4a6_gemm(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8
                  int K, int split_k, int split_mode, int out_dtype, int epilogue,
                  void* workspace, size_t workspace_bytes, bd_stream_t stream);
 
+/* Launch flags of bd_w4a6_gemm_ex. */
+#define BD_GEMM_OVERLAP_PREV 1u   /* may start while the previous kernel on the stream ends */
+#define BD_GEMM_WEIGHTS_STATIC 2u /* b / b_scales are not written by that previous kernel */
+
+/* bd_w4a6_gemm with launch flags (same arguments, same results).
+ * BD_GEMM_OVERLAP_PREV launches with programmatic stream serialisation: the kernel's CTAs may
+ * be scheduled as the previous kernel's CTAs retire (the previous kernel must allow it:
+ * bd_w4a6_gemm kernels do, other kernels start it only when they end). The kernel waits for
+ * the previous kernel to complete before it reads a, a_scales or bias and before it touches
+ * c or the workspace. With BD_GEMM_WEIGHTS_STATIC as well, it starts streaming b and
+ * b_scales before that wait, so the caller guarantees that the previous kernel does not
+ * write them (weights that stay resident across decode steps). No reference counterpart: the
+ * reference launches each GEMM on its own (kernel/bench_sweep.py:87-161). */
+int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8_t* b,
+                    const uint8_t* b_scales, float b_tensor_scale, const void* bias, int M, int N,
+                    int K, int split_k, int split_mode, int out_dtype, int epilogue,
+                    void* workspace, size_t workspace_bytes, unsigned flags, bd_stream_t stream);
+
 /* Sum of split_k fp32 partial planes (split_k, M, N) -> C (out dtype), times b_tensor_scale,
  * plus bias/activation. Replaces the torch.sum over planes in kernel/bench_sweep.py:141-142. */
 int bd_splitk_reduce(const float* partials, void* c, const void* bias, float b_tensor_scale,

@@ -27,8 +27,8 @@ def lib():
 
 def test_header_declares_the_entry_points():
     fns = declared_functions()
-    for f in ("bd_transcode_nvfp4_to_mxfp6", "bd_w4a6_gemm", "bd_splitk_reduce", "bd_pack_b",
-              "bd_pack_a", "bd_query_workspace"):
+    for f in ("bd_transcode_nvfp4_to_mxfp6", "bd_w4a6_gemm", "bd_w4a6_gemm_ex",
+              "bd_splitk_reduce", "bd_pack_b", "bd_pack_a", "bd_query_workspace"):
         assert f in fns
 
 
@@ -65,6 +65,17 @@ def test_gemm_rejects_bad_arguments_before_launch(lib):
     assert g(ok, P(4097), ok, ok, ok, 1.0, None, 16, 128, 128, 1, 0, 0, 0, None, 0, None) == -3
 
 
+def test_gemm_ex_validates_flags_then_arguments(lib):
+    P = ctypes.c_void_p
+    ok = P(4096)
+    g = lib.bd_w4a6_gemm_ex
+    # unknown flag bit
+    assert g(ok, ok, ok, ok, ok, 1.0, None, 16, 128, 128, 1, 0, 0, 0, None, 0, 4, None) == -1
+    # known flags, then the same checks as bd_w4a6_gemm
+    assert g(None, ok, ok, ok, ok, 1.0, None, 16, 128, 128, 1, 0, 0, 0, None, 0, 3, None) == -1
+    assert g(ok, ok, ok, ok, ok, 1.0, None, 16, 100, 128, 1, 0, 0, 0, None, 0, 1, None) == -2
+
+
 def test_transcode_rejects_bad_arguments(lib):
     P = ctypes.c_void_p
     ok = P(4096)
@@ -90,11 +101,15 @@ def test_workspace_query(lib):
     assert lib.bd_query_workspace(64, 1024, 1024, 4, 1) == 0   # planes need none
     assert lib.bd_query_workspace(64, 1024, 1024, 1, 0) == 0
     assert lib.bd_query_workspace(64, 1000, 1024, 4, 0) == 0   # invalid shape
-    # stream-K (split_k 0): slots for (grid x 2) partial tiles + one counter per tile; with no
-    # device visible the library assumes 148 SMs
-    tiles = 14336 // 128
-    slots = 148 * 2 * 16 * 128 * 4
+    # stream-K (split_k 0): slots for (grid x 2) partial tiles of 16 token rows x 256 weight
+    # rows + one counter per tile; with no device visible the library assumes 148 SMs
+    tiles = 14336 // 256
+    slots = 148 * 2 * 16 * 256 * 4
     assert lib.bd_query_workspace(16, 14336, 4096, 0, 0) == slots + (tiles * 4 + 255) // 256 * 256
+    # a small problem: grid = units = tiles x K/128 chunks
+    tiles, units = 2 * 1, 2 * 1 * 4
+    assert lib.bd_query_workspace(100, 384, 512, 0, 0) == \
+        units * 2 * 128 * 256 * 4 + (tiles * 4 + 255) // 256 * 256
 
 
 def test_psg_shim_validation_matches_reference_errors():

@@ -238,3 +238,41 @@ def test_workspace_reused_across_shapes():
         acts = bd.pack_activations(dev(ops[0]), dev(ops[1]))
         w = bd.pack_weights(dev(ops[2]), dev(ops[3]), 1.0)
         check(bd.w4a6_gemm(acts, w, workspace=ws), C, Cabs)
+
+
+@pytest.mark.parametrize("M", [1, 16, 64, 200])
+def test_overlapped_launch_chain(M):
+    """GEMMs launched with programmatic serialisation (bd_w4a6_gemm_ex flags): a chain where
+    every GEMM shares C and the stream-K workspace with the one before it, and where each
+    activation matrix is written by the kernel right before its GEMM, gives the same bytes as
+    the same chain launched one after another, and each matches the gold."""
+    import bitdance_b200 as bd
+    N, K = 1024, 2048
+    n_chain = 6
+    ops_list = [random_operands(M, N, K, seed=100 * M + i) for i in range(n_chain)]
+    ws = [bd.pack_weights(dev(op[2]), dev(op[3]), 0.5) for op in ops_list]
+    a_nat = [(dev(op[0]), dev(op[1])) for op in ops_list]
+    for overlap in (False, True):
+        wsp = bd.ops.Workspace()
+        out = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+        got = []
+        for i in range(n_chain):
+            acts = bd.pack_activations(*a_nat[i])          # written by the previous kernel
+            bd.w4a6_gemm(acts, ws[i], out=out, workspace=wsp, overlap_prev=overlap,
+                         weights_static=overlap)
+            bd.w4a6_gemm(acts, ws[(i + 1) % n_chain], out=out, workspace=wsp,
+                         overlap_prev=overlap, weights_static=overlap)
+            got.append(out.clone())
+        torch.cuda.synchronize()
+        assert bd.device_error() == 0
+        if not overlap:
+            ref = got
+        else:
+            for i in range(n_chain):
+                assert torch.equal(got[i], ref[i]), i
+    for i in (0, n_chain - 1):
+        a_codes, a_e8 = ops_list[i][0], ops_list[i][1]
+        b_packed, b_sc = ops_list[(i + 1) % n_chain][2], ops_list[(i + 1) % n_chain][3]
+        C, Cabs = gold(a_codes, a_e8, b_packed, b_sc, 0.5)
+        check(ref[i], C, Cabs)
+
