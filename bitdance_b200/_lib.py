@@ -44,6 +44,7 @@ SIGNATURES = {
     "bd_w4a6_gemm": (_I, [_P, _P, _P, _P, _P, _F, _P, _I, _I, _I, _I, _I, _I, _I, _P, _SZ, _P]),
     "bd_w4a6_gemm_ex": (_I, [_P, _P, _P, _P, _P, _F, _P, _I, _I, _I, _I, _I, _I, _I, _P, _SZ,
                              ctypes.c_uint, _P]),
+    "bd_w4a6_gemm_noalloc": (_I, [_P, _P, _P, _P, _P, _F, _P, _I, _I, _I, _I, _I, _P]),
     "bd_splitk_reduce": (_I, [_P, _P, _P, _F, _I, _I, _I, _I, _I, _P]),
 }
 

@@ -59,6 +59,30 @@ int device_info(DeviceInfo** out) {
   return d.is_sm100 ? BD_OK : BD_ERR_ARCH;
 }
 
+// Scratch of bd_w4a6_gemm_noalloc: the stream-K partial slots and per-tile counters of one
+// call live in this file-scope array instead of a caller-provided workspace, so that entry
+// point performs no device allocation. 16 MiB holds the stream-K scratch of every problem
+// with at most 32 token rows per tile on a 148-SM B200 (148 x 2 x 32 x 256 fp32 slots plus
+// counters); larger problems that need stream-K scratch are rejected.
+constexpr size_t kNoAllocScratchBytes = size_t{16} << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+void* g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device (looked up once per device, with
+// that device current).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BD_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) return BD_ERR_CUDA;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return BD_OK;
+}
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda needed).
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -411,6 +435,36 @@ int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const ui
   if (rc != BD_OK || !use_ws) return rc;
   return bd_splitk_reduce(static_cast<const float*>(workspace), c, bias, b_tensor_scale, M, N,
                           split_k, out_dtype, epilogue, stream);
+}
+
+int bd_w4a6_gemm_noalloc(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8_t* b,
+                         const uint8_t* b_scales, float b_tensor_scale, const void* bias, int M,
+                         int N, int K, int out_dtype, int epilogue, bd_stream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % 128) return BD_ERR_SHAPE;
+  DeviceInfo* d = nullptr;
+  int st = device_info(&d);
+  if (st != BD_OK) return st;
+  // the schedule bd_w4a6_gemm picks for split_k = 0: stream-K (needs the scratch) unless the
+  // tiles fill the machine twice over
+  const int bm = token_tile(M);
+  const int64_t tiles =
+      static_cast<int64_t>((N + kTileN - 1) / kTileN) * ((M + bm - 1) / bm);
+  void* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  if (tiles < 2 * d->sm_count) {
+    const StreamKSizes z = streamk_sizes(M, N, K, d->sm_count);
+    if (z.total > kNoAllocScratchBytes) return BD_ERR_WORKSPACE;
+    st = noalloc_scratch(&scratch);
+    if (st != BD_OK) return st;
+    // the tile counters must start at zero (a call that ran into a wait limit can leave them
+    // set); the slots need no clearing
+    if (cudaMemsetAsync(static_cast<uint8_t*>(scratch) + z.slots_bytes, 0, z.counter_bytes,
+                        as_stream(stream)) != cudaSuccess)
+      return BD_ERR_CUDA;
+    scratch_bytes = kNoAllocScratchBytes;
+  }
+  return bd_w4a6_gemm(c, a, a_scales, b, b_scales, b_tensor_scale, bias, M, N, K, 0,
+                      BD_SPLIT_REDUCE, out_dtype, epilogue, scratch, scratch_bytes, stream);
 }
 
 }  // extern "C"

@@ -189,6 +189,29 @@ def w4a6_gemm(acts: PackedActivations, weights: PackedWeights,
     return out
 
 
+def w4a6_gemm_noalloc(acts: PackedActivations, weights: PackedWeights, out: torch.Tensor,
+                      bias: Optional[torch.Tensor] = None, epilogue: str = "none",
+                      stream=None) -> torch.Tensor:
+    """w4a6_gemm (default schedule) through bd_w4a6_gemm_noalloc: no workspace and no device
+    allocation on this path (`out` is the caller's); its scratch is a static array in the
+    library shared by every call on the device, so calls must not overlap in time."""
+    M, K, N = acts.M, acts.K, weights.N
+    if weights.K != K:
+        raise ValueError(f"K mismatch: activations {K}, weights {weights.K}")
+    if out.dtype not in _OUT:
+        raise ValueError(f"unsupported output dtype {out.dtype}")
+    _need(out, out.dtype, "out", M * N)
+    if bias is not None:
+        _need(bias, torch.bfloat16, "bias", N)
+    epi = EPILOGUES[epilogue]
+    if epi != _lib.BD_EPI_NONE and bias is None:
+        raise ValueError(f"epilogue {epilogue!r} needs a bias")
+    call("bd_w4a6_gemm_noalloc", _p(out), _p(acts.codes), _p(acts.scales), _p(weights.codes),
+         _p(weights.scales), float(weights.tensor_scale), _p(bias), M, N, K, _OUT[out.dtype],
+         epi, _stream(stream))
+    return out
+
+
 def device_error(clear: bool = True) -> int:
     """Error word set by kernels whose bounded waits ran out (0 = none)."""
     w = ctypes.c_uint32(0)

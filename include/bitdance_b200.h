@@ -148,6 +148,23 @@ int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const ui
                     int K, int split_k, int split_mode, int out_dtype, int epilogue,
                     void* workspace, size_t workspace_bytes, unsigned flags, bd_stream_t stream);
 
+/* bd_w4a6_gemm with split_k = 0 (the default schedule) that allocates nothing and takes no
+ * workspace: the stream-K partial slots and tile counters live in a static 16 MiB device array
+ * inside the library. For callers that cannot allocate device memory at the call: hosts
+ * binding the C ABI without a device allocator of their own, and serving loops whose memory
+ * pool is sized up front, where an allocation could synchronise the device or fragment it.
+ * Limit: problems whose stream-K scratch (bd_query_workspace(M, N, K, 0, 0)) exceeds 16 MiB
+ * return BD_ERR_WORKSPACE (on a 148-SM B200 every problem with M <= 32 fits; problems whose
+ * tiles fill the machine twice over need no scratch and always run). Every call clears the
+ * tile counters with cudaMemsetAsync on `stream` before the kernel. All calls on a device share
+ * the one array: calls that overlap in time (other streams, other threads) race and give
+ * wrong results. The first call on each device performs one-time set-up (symbol lookup, kernel
+ * attributes); make it before any stream capture. Same results as bd_w4a6_gemm. No reference
+ * counterpart (the reference allocates its buffers in Python, kernel/bench_sweep.py:59-85). */
+int bd_w4a6_gemm_noalloc(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8_t* b,
+                         const uint8_t* b_scales, float b_tensor_scale, const void* bias, int M,
+                         int N, int K, int out_dtype, int epilogue, bd_stream_t stream);
+
 /* Sum of split_k fp32 partial planes (split_k, M, N) -> C (out dtype), times b_tensor_scale,
  * plus bias/activation. Replaces the torch.sum over planes in kernel/bench_sweep.py:141-142. */
 int bd_splitk_reduce(const float* partials, void* c, const void* bias, float b_tensor_scale,
