@@ -19,10 +19,11 @@
 //                                and E4M3 scales (2 x 1 KB) into the weight ring (deep).
 //   warp 22     token producer   TMA: token rows (128B-swizzled packed E2M3) and their E8M0
 //                                scales into the token ring.
-//   warps 6..21 transcode        16 warps; thread (warp w, lane l) converts weight row
-//                                16w + (l & 15), K blocks 2(l >> 4) and 2(l >> 4) + 1 of a
-//                                chunk into E4M3 bytes of the 128B-swizzled operand tile in
-//                                shared memory (the B ring) and stages the row's E8M0 scales.
+//   warps 6..21 transcode        two groups of 8 warps taking alternate chunks (two chunks in
+//                                flight); thread (warp gw of its group, lane l) converts the
+//                                four K blocks of weight row 32 gw + l into
+//                                E4M3 bytes of the 128B-swizzled operand tile in shared memory
+//                                (the B ring) and stages the rows' E8M0 scales.
 //   warp 1      MMA              4 block-scaled tcgen05.mma per chunk (both operands from
 //                                shared memory); its commits free the B and token slots.
 //   warps 2..5  epilogue         per chunk: token and weight scale factors into tensor memory
@@ -47,16 +48,17 @@ constexpr int cround(int x, int a) { return (x + a - 1) / a * a; }
 
 constexpr int kTileN = 256;  // weight rows per tile (the MMA's N)
 
-// Ring depths per token rows BM: weight ring SW (raw NVFP4, released by the transcode warps
-// once in registers), B ring SB (transcoded operand, released by the MMA), token ring ST.
+// Ring depths per token rows BM: weight ring SW (raw NVFP4 in shared memory, released by the
+// transcode warps), B ring SB (transcoded operand, released by the MMA), token ring ST, and G,
+// the number of transcode warp groups that take chunks in turn. SW and SB are multiples of G,
+// so a slot is only ever used by one group, in order: no waiter can run a whole phase ahead.
 struct RingDepths {
-  int sw, sb, st;
+  int sw, sb, st, groups;
 };
 constexpr RingDepths ring_depths(int BM) {
-  if (BM <= 16) return {6, 3, 4};
-  if (BM <= 32) return {5, 3, 4};
-  if (BM <= 64) return {5, 3, 3};
-  return {4, 3, 3};
+  if (BM <= 16) return {4, 4, 4, 2};
+  if (BM <= 32) return {4, 4, 2, 2};
+  return {4, 2, 3, 2};
 }
 
 template <int BM>
@@ -64,6 +66,7 @@ struct GemmCfg {
   static constexpr int SW = ring_depths(BM).sw;
   static constexpr int SB = ring_depths(BM).sb;
   static constexpr int ST = ring_depths(BM).st;
+  static constexpr int kGroups = ring_depths(BM).groups;  // transcode warp groups
   // token stage: BM rows x 128 B (128B-swizzled), then BM E8M0 words. The MMA reads 128 rows
   // from the slot base; rows >= BM lie in the buffers that follow (their values are unused:
   // they only reach accumulator lanes >= BM, which are never stored).
@@ -79,7 +82,10 @@ struct GemmCfg {
   static constexpr int oW = ST * kTStage;
   static constexpr int oB = oW + SW * kWStage;
   static constexpr int oSf = oB + SB * kBStage;  // SB x 256 E8M0 words staged for tensor memory
-  static constexpr int oCtl = oSf + SB * 1024;
+  // magnitude table, 16 copies interleaved (entry e of copy j at e*128 + j*8): lane l reads
+  // copy l % 16, so a warp's lookups never conflict
+  static constexpr int oPerm = oSf + SB * 1024;
+  static constexpr int oCtl = oPerm + 64 * 128;
   static constexpr int kCtlBytes = 2048;
   static constexpr int kSmemBytes = oCtl + kCtlBytes + 1024;  // + alignment slack
   // tensor memory: accumulator (256 columns) | per B slot 12 scale columns: 4 token (A)
@@ -89,6 +95,8 @@ struct GemmCfg {
   static constexpr int kSfCol0 = 256;
   static constexpr int kTmemCols = 512;
   static constexpr int kTranscodeWarps = 16;
+  static constexpr int kGroupWarps = kTranscodeWarps / kGroups;
+  static constexpr int kRowsPerThread = 256 / (32 * kGroupWarps);
   static constexpr int kEpiWarps = 4;
   static constexpr int kTProducerWarp = 2 + kEpiWarps + kTranscodeWarps;  // 22
   static constexpr int kThreads = 32 * (kTProducerWarp + 1);
@@ -98,6 +106,7 @@ struct GemmCfg {
   static_assert(kSfCols % 4 == 0 && kSfCol0 % 4 == 0, "scale-factor addresses 4-column aligned");
   static_assert(oW % 1024 == 0 && oB % 1024 == 0 && kTStage % 1024 == 0, "1 KB swizzle atoms");
   static_assert(SW <= 8 && SB <= 4 && ST <= 4, "control block sizes");
+  static_assert(SW % kGroups == 0 && SB % kGroups == 0, "slots owned by one group");
 };
 
 struct GemmCtl {
@@ -178,6 +187,37 @@ struct Schedule {
     return true;
   }
 };
+
+// Magnitude-table rows (d*8 + mb) of the two 16-blocks of a 32-block and its E8M0 byte, from
+// the two E4M3 scale bytes. A normal scale byte s has mantissa bits s & 7 and bumped exponent
+// e = ((s & 0x7F) + 7) / 8 - 7 (exponent field + (mantissa != 0) - 7), so only subnormal and
+// zero scales read the class table.
+__device__ __forceinline__ void pair_class(const TranscodeTables& t, uint32_t s0, uint32_t s1,
+                                           uint32_t& i0, uint32_t& i1, uint32_t& e8) {
+  const uint32_t x0 = s0 & 0x7Fu, x1 = s1 & 0x7Fu;
+  int ep0, ep1;  // e + 7
+  uint32_t mb0, mb1;
+  if (x0 & 0x78u) {
+    ep0 = static_cast<int>((x0 + 7u) >> 3);
+    mb0 = x0 & 7u;
+  } else {
+    const uint32_t v = t.info[x0];
+    ep0 = static_cast<int>(v >> 3) - 9;
+    mb0 = v & 7u;
+  }
+  if (x1 & 0x78u) {
+    ep1 = static_cast<int>((x1 + 7u) >> 3);
+    mb1 = x1 & 7u;
+  } else {
+    const uint32_t v = t.info[x1];
+    ep1 = static_cast<int>(v >> 3) - 9;
+    mb1 = v & 7u;
+  }
+  const int em = max(ep0, ep1);
+  i0 = static_cast<uint32_t>(min(em - ep0, 7)) * 8u + mb0;
+  i1 = static_cast<uint32_t>(min(em - ep1, 7)) * 8u + mb1;
+  e8 = static_cast<uint32_t>(em + 120);  // e + 127
+}
 
 __device__ __forceinline__ float apply_epilogue(float v, int epi, const __nv_bfloat16* bias,
                                                 int n) {
@@ -357,7 +397,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
     ctl.abort_flag = 0;
     for (int s = 0; s < Cfg::SW; ++s) {
       mbar_init(smem_u32(&ctl.wfull[s]), 1);
-      mbar_init(smem_u32(&ctl.wempty[s]), Cfg::kTranscodeWarps);
+      mbar_init(smem_u32(&ctl.wempty[s]), Cfg::kGroupWarps);
     }
     for (int s = 0; s < Cfg::ST; ++s) {
       mbar_init(smem_u32(&ctl.tfull[s]), 1);
@@ -366,7 +406,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
     for (int s = 0; s < Cfg::SB; ++s) {
       mbar_init(smem_u32(&ctl.bready[s]), Cfg::kEpiWarps);
       mbar_init(smem_u32(&ctl.bempty[s]), 1);
-      mbar_init(smem_u32(&ctl.sfready[s]), Cfg::kTranscodeWarps);
+      mbar_init(smem_u32(&ctl.sfready[s]), Cfg::kGroupWarps);
     }
     mbar_init(smem_u32(&ctl.acc_full), 1);
     mbar_init(smem_u32(&ctl.acc_empty), Cfg::kEpiWarps);
@@ -388,7 +428,11 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
       tmem_alloc(smem_u32(&ctl.tmem_base), Cfg::kTmemCols);
       tmem_relinquish();
     } else if (warp >= 2 + Cfg::kEpiWarps) {
-      load_tables<true>(ctl.tab, tid - 32 * (2 + Cfg::kEpiWarps), 32 * Cfg::kTranscodeWarps);
+      const int t0 = tid - 32 * (2 + Cfg::kEpiWarps);
+      load_tables<true>(ctl.tab, t0, 32 * Cfg::kTranscodeWarps);
+      const uint2* src = reinterpret_cast<const uint2*>(&g_tables_e4m3);  // perm[] comes first
+      uint2* rep = reinterpret_cast<uint2*>(smem + Cfg::oPerm);
+      for (int i = t0; i < 64 * 16; i += 32 * Cfg::kTranscodeWarps) rep[i] = __ldg(src + (i >> 4));
     }
     tc_fence_before();
     named_barrier(2, 32 * (Cfg::kTProducerWarp - 1));
@@ -492,71 +536,78 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
     }
   } else if (warp >= 2 + Cfg::kEpiWarps) {
     // ------------------------------------------------------------------ transcode
+    // The 16 warps form kGroups groups that take alternate chunks, so several chunks are in
+    // flight at once; in a group, thread (warp gw, lane) converts all four K blocks of weight
+    // row 32 gw + lane.
     const int tw = warp - 2 - Cfg::kEpiWarps;  // 0..15
-    const int row = tw * 16 + (lane & 15);     // weight row of the tile
-    const int hk = lane >> 4;                  // K blocks 2hk, 2hk + 1 of each chunk
-    const int rr = row & 127;
-    const int half_off = (row >> 7) * 8192;
-    // raw codes: 64B-swizzled 128-row halves, 16-byte chunk c of row rr at
-    // rr*64 + ((c ^ ((rr >> 1) & 3)) << 4); chunk c holds K block c
-    const int code_off0 = half_off + rr * 64 + (((2 * hk) ^ ((rr >> 1) & 3)) << 4);
-    const int code_off1 = half_off + rr * 64 + (((2 * hk + 1) ^ ((rr >> 1) & 3)) << 4);
-    const int scale_off = Cfg::kWCodes + (row >> 7) * 1024 + rr * 8 + hk * 4;
-    // B operand: 128B-swizzled K-major, 16-byte chunk cc of row r at
-    // (r >> 3)*1024 + (r & 7)*128 + ((cc ^ (r & 7)) << 4); block b covers chunks 2b, 2b + 1
-    const int b_row = (row >> 3) * 1024 + (row & 7) * 128;
-    const int r7 = row & 7;
-    RingPos<Cfg::SW> w;
-    RingPos<Cfg::SB> b;
+    const int grp = tw / Cfg::kGroupWarps;
+    constexpr int R = Cfg::kRowsPerThread;
+    // rows of this thread: 32 (tw % group warps) + lane + 32 * group warps * r
+    int code_row[R], scale_off[R], b_row[R], sw[R], r7[R], rows[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int row = r * (32 * Cfg::kGroupWarps) + (tw % Cfg::kGroupWarps) * 32 + lane;
+      const int rr = row & 127;
+      rows[r] = row;
+      // raw codes: 64B-swizzled 128-row halves, 16-byte chunk c of row rr at
+      // rr*64 + ((c ^ ((rr >> 1) & 3)) << 4); chunk c holds K block c
+      code_row[r] = (row >> 7) * 8192 + rr * 64;
+      sw[r] = (rr >> 1) & 3;
+      scale_off[r] = Cfg::kWCodes + (row >> 7) * 1024 + rr * 8;
+      // B operand: 128B-swizzled K-major, 16-byte chunk cc of row n at
+      // (n >> 3)*1024 + (n & 7)*128 + ((cc ^ (n & 7)) << 4); block b covers chunks 2b, 2b + 1
+      b_row[r] = (row >> 3) * 1024 + (row & 7) * 128;
+      r7[r] = row & 7;
+    }
+    const uint8_t* perm = smem + Cfg::oPerm + (lane & 15) * 8;
+    int ci = 0;  // chunk number within this CTA
     Seg sg;
     for (int idx = 0; sch.segment(cta, idx, sg) && !*abort_flag; ++idx) {
-      for (int k = sg.k0; k < sg.k1; ++k) {
-        if (!mbar_wait(smem_u32(&ctl.wfull[w.slot]), w.phase, p.err, kErrWaitTma, abort_flag))
-          break;
-        const uint8_t* st = smem + Cfg::oW + w.slot * Cfg::kWStage;
-        const uint4 q0 = *reinterpret_cast<const uint4*>(st + code_off0);
-        const uint4 q1 = *reinterpret_cast<const uint4*>(st + code_off1);
-        const uint32_t sc = *reinterpret_cast<const uint32_t*>(st + scale_off);
+      for (int k = sg.k0; k < sg.k1; ++k, ++ci) {
+        if (ci % Cfg::kGroups != grp) continue;
+        const int ws = ci % Cfg::SW, bs = ci % Cfg::SB;
+        const uint32_t wph = (ci / Cfg::SW) & 1, bph = (ci / Cfg::SB) & 1;
+        if (!mbar_wait(smem_u32(&ctl.wfull[ws]), wph, p.err, kErrWaitTma, abort_flag)) break;
+        const uint8_t* st = smem + Cfg::oW + ws * Cfg::kWStage;
+        uint4 q[R][4];
+        uint2 sc[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            q[r][c] = *reinterpret_cast<const uint4*>(st + code_row[r] + ((c ^ sw[r]) << 4));
+          sc[r] = *reinterpret_cast<const uint2*>(st + scale_off[r]);
+        }
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&ctl.wempty[w.slot]));
-        w.next();
-        uint32_t v0[8], v1[8];
-        uint32_t e0, e1;
-        {
-          uint2 T0, T1;
-          scale_pair(ctl.tab, sc & 0xFFu, (sc >> 8) & 0xFFu, T0, T1, e0);
-          nib8_to_e4m3(q0.x, T0, v0[0], v0[1]);
-          nib8_to_e4m3(q0.y, T0, v0[2], v0[3]);
-          nib8_to_e4m3(q0.z, T1, v0[4], v0[5]);
-          nib8_to_e4m3(q0.w, T1, v0[6], v0[7]);
-        }
-        {
-          uint2 T0, T1;
-          scale_pair(ctl.tab, (sc >> 16) & 0xFFu, sc >> 24, T0, T1, e1);
-          nib8_to_e4m3(q1.x, T0, v1[0], v1[1]);
-          nib8_to_e4m3(q1.y, T0, v1[2], v1[3]);
-          nib8_to_e4m3(q1.z, T1, v1[4], v1[5]);
-          nib8_to_e4m3(q1.w, T1, v1[6], v1[7]);
-        }
-        // E8M0 word of this row: blocks 0..3 in bytes 0..3 (lanes l and l ^ 16 share the row)
-        const uint32_t mine = e0 | (e1 << 8);
-        const uint32_t other = __shfl_xor_sync(0xFFFFFFFFu, mine, 16);
-        const uint32_t sfw = hk == 0 ? (mine | (other << 16)) : (other | (mine << 16));
-        if (!mbar_wait(smem_u32(&ctl.bempty[b.slot]), b.phase ^ 1u, p.err, kErrWaitMma,
-                       abort_flag))
+        if (lane == 0) mbar_arrive(smem_u32(&ctl.wempty[ws]));
+        if (!mbar_wait(smem_u32(&ctl.bempty[bs]), bph ^ 1u, p.err, kErrWaitMma, abort_flag))
           break;
-        const uint32_t bt = smem_u32(smem + Cfg::oB + b.slot * Cfg::kBStage) + b_row;
-        const int c0 = 4 * hk;  // first 16-byte chunk of block 2hk
-        st_shared_v4(bt + (((c0 + 0) ^ r7) << 4), v0[0], v0[1], v0[2], v0[3]);
-        st_shared_v4(bt + (((c0 + 1) ^ r7) << 4), v0[4], v0[5], v0[6], v0[7]);
-        st_shared_v4(bt + (((c0 + 2) ^ r7) << 4), v1[0], v1[1], v1[2], v1[3]);
-        st_shared_v4(bt + (((c0 + 3) ^ r7) << 4), v1[4], v1[5], v1[6], v1[7]);
-        uint32_t* sf_stage = reinterpret_cast<uint32_t*>(smem + Cfg::oSf + b.slot * 1024);
-        if (hk == 0) sf_stage[row] = sfw;
+        const uint32_t bt = smem_u32(smem + Cfg::oB + bs * Cfg::kBStage);
+        uint32_t* sf_stage = reinterpret_cast<uint32_t*>(smem + Cfg::oSf + bs * 1024);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          uint32_t sfw = 0;
+#pragma unroll
+          for (int blk = 0; blk < 4; ++blk) {
+            const uint32_t pair = blk < 2 ? (sc[r].x >> (16 * blk)) : (sc[r].y >> (16 * (blk - 2)));
+            uint32_t i0, i1, e8;
+            pair_class(ctl.tab, pair & 0xFFu, (pair >> 8) & 0xFFu, i0, i1, e8);
+            const uint2 T0 = *reinterpret_cast<const uint2*>(perm + i0 * 128);
+            const uint2 T1 = *reinterpret_cast<const uint2*>(perm + i1 * 128);
+            uint32_t v[8];
+            nib8_to_e4m3(q[r][blk].x, T0, v[0], v[1]);
+            nib8_to_e4m3(q[r][blk].y, T0, v[2], v[3]);
+            nib8_to_e4m3(q[r][blk].z, T1, v[4], v[5]);
+            nib8_to_e4m3(q[r][blk].w, T1, v[6], v[7]);
+            st_shared_v4(bt + b_row[r] + (((2 * blk) ^ r7[r]) << 4), v[0], v[1], v[2], v[3]);
+            st_shared_v4(bt + b_row[r] + (((2 * blk + 1) ^ r7[r]) << 4), v[4], v[5], v[6], v[7]);
+            sfw |= e8 << (8 * blk);
+          }
+          sf_stage[rows[r]] = sfw;
+        }
         fence_proxy_async_smem();  // the tensor core reads the B tile through the async proxy
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&ctl.sfready[b.slot]));
-        b.next();
+        if (lane == 0) mbar_arrive(smem_u32(&ctl.sfready[bs]));
       }
     }
     // the fix-up of the tile of this CTA's last segment, when this CTA finishes it, is shared
