@@ -2,9 +2,10 @@
 //
 // One block-scaled tcgen05.mma (kind::mxf8f6f4, M = 128, K = 32) costs the tensor core the
 // same time whatever its N (16..256), so the weights are the MMA's N operand, 256 rows per
-// MMA, and the tokens are its M operand (128 rows; a decode batch loads only its BM <= 128
-// token rows and leaves the rest of the operand unused). Output tile: BM tokens x 256 weight
-// rows, accumulated in tensor memory as 128 lanes (tokens) x 256 fp32 columns (weight rows).
+// MMA, and the tokens are its M operand, read from tensor memory (128 lanes; a decode batch
+// writes only its BM <= 128 token rows, no MMA read ever touches memory a copy may be
+// writing). Output tile: BM tokens x 256 weight rows, accumulated in tensor memory as 128
+// lanes (tokens) x 256 fp32 columns (weight rows).
 //
 // Persistent CTAs walk a schedule of "segments" (a tile and a range of 128-wide K chunks):
 //   * stream-K (the default): the (tile, K chunk) units are cut into one contiguous range per
@@ -17,17 +18,20 @@
 // Warp roles (736 threads):
 //   warp 0      weight producer  TMA: packed NVFP4 codes (2 x 8 KB per chunk, 64B-swizzled)
 //                                and E4M3 scales (2 x 1 KB) into the weight ring (deep).
-//   warp 22     token producer   TMA: token rows (128B-swizzled packed E2M3) and their E8M0
-//                                scales into the token ring.
+//   warp 22     token producer   TMA: token rows (one E2M3 code per byte, 128B-swizzled) and
+//                                their E8M0 scales into the token ring.
 //   warps 6..21 transcode        two groups of 8 warps taking alternate chunks (two chunks in
 //                                flight); thread (warp gw of its group, lane l) converts the
 //                                four K blocks of weight row 32 gw + l into
 //                                E4M3 bytes of the 128B-swizzled operand tile in shared memory
 //                                (the B ring) and stages the rows' E8M0 scales.
-//   warp 1      MMA              4 block-scaled tcgen05.mma per chunk (both operands from
-//                                shared memory); its commits free the B and token slots.
-//   warps 2..5  epilogue         per chunk: token and weight scale factors into tensor memory
-//                                (tcgen05.st, one warp per lane quarter); per segment:
+//   warp 1      MMA              4 block-scaled tcgen05.mma per chunk (A = tokens from tensor
+//                                memory, B = transcoded weights from shared memory); its
+//                                commits free the B and token slots.
+//   warps 2..5  epilogue         per chunk (one warp per tensor-memory lane quarter): the
+//                                quarter's token rows (the MMA's A operand) and the token and
+//                                weight scale factors into tensor memory (tcgen05.st); per
+//                                segment:
 //                                tensor-memory accumulator -> registers -> C / partials.
 #pragma once
 #include <cuda_bf16.h>
@@ -56,9 +60,10 @@ struct RingDepths {
   int sw, sb, st, groups;
 };
 constexpr RingDepths ring_depths(int BM) {
-  if (BM <= 16) return {4, 4, 4, 2};
-  if (BM <= 32) return {4, 4, 2, 2};
-  return {4, 2, 3, 2};
+  if (BM <= 16) return {4, 4, 8, 2};
+  if (BM <= 32) return {4, 4, 4, 2};
+  if (BM <= 64) return {4, 2, 6, 2};
+  return {4, 2, 4, 2};
 }
 
 template <int BM>
@@ -67,32 +72,38 @@ struct GemmCfg {
   static constexpr int SB = ring_depths(BM).sb;
   static constexpr int ST = ring_depths(BM).st;
   static constexpr int kGroups = ring_depths(BM).groups;  // transcode warp groups
-  // token stage: BM rows x 128 B (128B-swizzled), then BM E8M0 words. The MMA reads 128 rows
-  // from the slot base; rows >= BM lie in the buffers that follow (their values are unused:
-  // they only reach accumulator lanes >= BM, which are never stored).
+  // token ring: BM rows x 128 B per slot (one E2M3 code per byte, 128B-swizzled so the copy
+  // into tensor memory reads without bank conflicts), and the BM E8M0 words of each slot in a
+  // separate small ring.
   static constexpr int kTRowBytes = BM * 128;
-  static constexpr int kTStage = cround(BM * 128 + BM * 4, 1024);
-  static constexpr int kTTx = BM * 128 + BM * 4;
+  static constexpr int kTScaleBytes = BM * 4;
+  static constexpr int kTScaleSlot = cround(kTScaleBytes, 128);  // TMA destinations: 128 B aligned
+  static constexpr int kTTx = kTRowBytes + kTScaleBytes;
   // weight stage: two 128-row halves x (8 KB codes, 64B-swizzled), then 2 x 1 KB scales
   static constexpr int kWCodes = 16384;
   static constexpr int kWStage = 16384 + 2048;
   // B stage: 256 rows x 128 B E4M3 (128B-swizzled, K-major)
   static constexpr int kBStage = 32768;
   static constexpr int oT = 0;
-  static constexpr int oW = ST * kTStage;
+  static constexpr int oW = ST * kTRowBytes;
   static constexpr int oB = oW + SW * kWStage;
   static constexpr int oSf = oB + SB * kBStage;  // SB x 256 E8M0 words staged for tensor memory
-  // magnitude table, 16 copies interleaved (entry e of copy j at e*128 + j*8): lane l reads
-  // copy l % 16, so a warp's lookups never conflict
+  // magnitude table, 8 copies interleaved (entry e of copy j at e*64 + j*8): lane l reads
+  // copy l % 8
+  static constexpr int kPermCopies = 8;
   static constexpr int oPerm = oSf + SB * 1024;
-  static constexpr int oCtl = oPerm + 64 * 128;
-  static constexpr int kCtlBytes = 2048;
+  static constexpr int oTs = oPerm + 64 * 8 * kPermCopies;  // token scale ring
+  static constexpr int oCtl = oTs + ST * kTScaleSlot;
+  static constexpr int kCtlBytes = 1024;
   static constexpr int kSmemBytes = oCtl + kCtlBytes + 1024;  // + alignment slack
-  // tensor memory: accumulator (256 columns) | per B slot 12 scale columns: 4 token (A)
-  // columns (lane m reads column m / 32) then 8 weight (B) columns (row n at lane n % 32 of
-  // every lane quarter, column n / 32)
+  // tensor memory: accumulator (256 columns) | per B slot the A operand (token m at lane m,
+  // 32 columns = 128 K codes) | per B slot 12 scale columns: 4 token (A) columns (lane m reads
+  // column m / 32) then 8 weight (B) columns (row n at lane n % 32 of every lane quarter,
+  // column n / 32). Lanes >= BM of the A slot are never written; they only reach accumulator
+  // lanes >= BM, which are never stored.
+  static constexpr int kACol0 = 256;
   static constexpr int kSfCols = 12;
-  static constexpr int kSfCol0 = 256;
+  static constexpr int kSfCol0 = kACol0 + 32 * SB;
   static constexpr int kTmemCols = 512;
   static constexpr int kTranscodeWarps = 16;
   static constexpr int kGroupWarps = kTranscodeWarps / kGroups;
@@ -101,16 +112,17 @@ struct GemmCfg {
   static constexpr int kTProducerWarp = 2 + kEpiWarps + kTranscodeWarps;  // 22
   static constexpr int kThreads = 32 * (kTProducerWarp + 1);
   static_assert(kSmemBytes <= 232448, "shared memory budget");
-  static_assert((ST - 1) * kTStage + 16384 <= oCtl, "token operand reads stay in the buffers");
   static_assert(kSfCol0 + SB * kSfCols <= kTmemCols, "tensor memory budget");
   static_assert(kSfCols % 4 == 0 && kSfCol0 % 4 == 0, "scale-factor addresses 4-column aligned");
-  static_assert(oW % 1024 == 0 && oB % 1024 == 0 && kTStage % 1024 == 0, "1 KB swizzle atoms");
-  static_assert(SW <= 8 && SB <= 4 && ST <= 4, "control block sizes");
+  static_assert(oW % 1024 == 0 && oB % 1024 == 0 && kTRowBytes % 1024 == 0, "1 KB swizzle atoms");
+  static_assert(oTs % 128 == 0 && kTScaleSlot % 128 == 0 && kWCodes % 128 == 0,
+                "TMA shared-memory destinations 128-byte aligned");
+  static_assert(SW <= 4 && SB <= 4 && ST <= 8, "control block sizes");
   static_assert(SW % kGroups == 0 && SB % kGroups == 0, "slots owned by one group");
 };
 
 struct GemmCtl {
-  uint64_t wfull[8], wempty[8], tfull[4], tempty[4], bready[4], bempty[4], sfready[4];
+  uint64_t wfull[4], wempty[4], tfull[8], tempty[8], bready[4], bempty[4], sfready[4];
   uint64_t acc_full, acc_empty, drain, fin_bar;
   uint32_t tmem_base;
   uint32_t fin_job;  // 1: this CTA finishes the tile of its last segment
@@ -383,6 +395,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
                      const __grid_constant__ CUtensorMap tm_w,
                      const __grid_constant__ CUtensorMap tm_ws, const GemmParams p) {
   using Cfg = GemmCfg<BM>;
+  static_assert(sizeof(GemmCtl) <= Cfg::kCtlBytes, "control block");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   GemmCtl& ctl = *reinterpret_cast<GemmCtl*>(smem + Cfg::oCtl);
@@ -432,7 +445,8 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
       load_tables<true>(ctl.tab, t0, 32 * Cfg::kTranscodeWarps);
       const uint2* src = reinterpret_cast<const uint2*>(&g_tables_e4m3);  // perm[] comes first
       uint2* rep = reinterpret_cast<uint2*>(smem + Cfg::oPerm);
-      for (int i = t0; i < 64 * 16; i += 32 * Cfg::kTranscodeWarps) rep[i] = __ldg(src + (i >> 4));
+      for (int i = t0; i < 64 * Cfg::kPermCopies; i += 32 * Cfg::kTranscodeWarps)
+        rep[i] = __ldg(src + i / Cfg::kPermCopies);
     }
     tc_fence_before();
     named_barrier(2, 32 * (Cfg::kTProducerWarp - 1));
@@ -485,11 +499,12 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
           if (!mbar_wait(smem_u32(&ctl.tempty[t.slot]), t.phase ^ 1u, p.err, kErrWaitEmpty,
                          abort_flag))
             break;
-          uint8_t* st = smem + Cfg::oT + t.slot * Cfg::kTStage;
+          uint8_t* st = smem + Cfg::oT + t.slot * Cfg::kTRowBytes;
           const uint32_t fb = smem_u32(&ctl.tfull[t.slot]);
           mbar_arrive_expect_tx(fb, Cfg::kTTx);
           tma_load_3d(smem_u32(st), &tm_a, 0, mt * BM, k, fb);
-          tma_load_2d(smem_u32(st + Cfg::kTRowBytes), &tm_as, mt * BM, k, fb);
+          tma_load_2d(smem_u32(smem + Cfg::oTs + t.slot * Cfg::kTScaleSlot), &tm_as, mt * BM, k,
+                      fb);
           t.next();
         }
       }
@@ -507,21 +522,22 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         tc_fence_after();
         bool ok = true;
         for (int k = sg.k0; k < sg.k1; ++k) {
+          // bready: the B tile, its scales and the token operand (copied into tensor memory
+          // after the token slot landed) are all in place
           if (!mbar_wait(smem_u32(&ctl.bready[b.slot]), b.phase, p.err, kErrWaitOperand,
-                         abort_flag) ||
-              !mbar_wait(smem_u32(&ctl.tfull[t.slot]), t.phase, p.err, kErrWaitTma, abort_flag)) {
+                         abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + Cfg::oT + t.slot * Cfg::kTStage);
           const uint32_t b_addr = smem_u32(smem + Cfg::oB + b.slot * Cfg::kBStage);
+          const uint32_t ta = tbase + Cfg::kACol0 + b.slot * 32;
           const uint32_t sfa = tbase + Cfg::kSfCol0 + b.slot * Cfg::kSfCols;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint32_t idesc = idesc_mxf8f6f4(128, kTileN, kFmtE2M3, kFmtE4M3, kk, kk);
-            mma_mxf8f6f4_ss(tbase, sdesc_sw128(a_addr + kk * 32), sdesc_sw128(b_addr + kk * 32),
-                            idesc, sfa, sfa + 4, (k == sg.k0 && kk == 0) ? 0u : 1u);
+            mma_mxf8f6f4_ts(tbase, ta + kk * 8, sdesc_sw128(b_addr + kk * 32), idesc, sfa, sfa + 4,
+                            (k == sg.k0 && kk == 0) ? 0u : 1u);
           }
           tc_commit(smem_u32(&ctl.bempty[b.slot]));
           tc_commit(smem_u32(&ctl.tempty[t.slot]));
@@ -559,7 +575,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
       b_row[r] = (row >> 3) * 1024 + (row & 7) * 128;
       r7[r] = row & 7;
     }
-    const uint8_t* perm = smem + Cfg::oPerm + (lane & 15) * 8;
+    const uint8_t* perm = smem + Cfg::oPerm + (lane % Cfg::kPermCopies) * 8;
     int ci = 0;  // chunk number within this CTA
     Seg sg;
     for (int idx = 0; sch.segment(cta, idx, sg) && !*abort_flag; ++idx) {
@@ -592,8 +608,8 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
             const uint32_t pair = blk < 2 ? (sc[r].x >> (16 * blk)) : (sc[r].y >> (16 * (blk - 2)));
             uint32_t i0, i1, e8;
             pair_class(ctl.tab, pair & 0xFFu, (pair >> 8) & 0xFFu, i0, i1, e8);
-            const uint2 T0 = *reinterpret_cast<const uint2*>(perm + i0 * 128);
-            const uint2 T1 = *reinterpret_cast<const uint2*>(perm + i1 * 128);
+            const uint2 T0 = *reinterpret_cast<const uint2*>(perm + i0 * (8 * Cfg::kPermCopies));
+            const uint2 T1 = *reinterpret_cast<const uint2*>(perm + i1 * (8 * Cfg::kPermCopies));
             uint32_t v[8];
             nib8_to_e4m3(q[r][blk].x, T0, v[0], v[1]);
             nib8_to_e4m3(q[r][blk].y, T0, v[2], v[3]);
@@ -649,8 +665,28 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
           ok = false;
           break;
         }
+        if (quarter * 32 < BM) {
+          // token rows of this lane quarter -> tensor-memory A slot (lane m = token m)
+          uint32_t av[32];
+          if (mrow < BM) {
+            const uint8_t* trow = smem + Cfg::oT + t.slot * Cfg::kTRowBytes + (mrow >> 3) * 1024 +
+                                  (mrow & 7) * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const uint4 v = *reinterpret_cast<const uint4*>(trow + ((c ^ (mrow & 7)) << 4));
+              av[4 * c + 0] = v.x & 0x3F3F3F3Fu;
+              av[4 * c + 1] = v.y & 0x3F3F3F3Fu;
+              av[4 * c + 2] = v.z & 0x3F3F3F3Fu;
+              av[4 * c + 3] = v.w & 0x3F3F3F3Fu;
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) av[c] = 0u;
+          }
+          tmem_st_x32(taddr + Cfg::kACol0 + b.slot * 32, av);
+        }
         const uint32_t* tok = reinterpret_cast<const uint32_t*>(
-            smem + Cfg::oT + t.slot * Cfg::kTStage + Cfg::kTRowBytes);
+            smem + Cfg::oTs + t.slot * Cfg::kTScaleSlot);
         const uint32_t tokw = mrow < BM ? tok[mrow] : 0u;
         const uint32_t* sf_stage = reinterpret_cast<const uint32_t*>(smem + Cfg::oSf + b.slot * 1024);
         uint32_t wv[8];

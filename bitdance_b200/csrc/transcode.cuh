@@ -217,18 +217,8 @@ __global__ void pack_a_codes_kernel(const uint8_t* __restrict__ codes, uint8_t* 
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nchunks;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const uint4 v = reinterpret_cast<const uint4*>(codes)[i];
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    uint64_t lo = 0, hi = 0;
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const uint64_t c = (w[e >> 2] >> (8 * (e & 3))) & 0x3Fu;
-      const int bit = 6 * e;
-      if (bit < 64) lo |= c << bit;
-      if (bit + 6 > 64) hi |= (bit >= 64) ? (c << (bit - 64)) : (c >> (64 - bit));
-    }
-    reinterpret_cast<uint4*>(out)[i] =
-        make_uint4(static_cast<uint32_t>(lo), static_cast<uint32_t>(lo >> 32),
-                   static_cast<uint32_t>(hi), 0u);
+    reinterpret_cast<uint4*>(out)[i] = make_uint4(v.x & 0x3F3F3F3Fu, v.y & 0x3F3F3F3Fu,
+                                                  v.z & 0x3F3F3F3Fu, v.w & 0x3F3F3F3Fu);
   }
 }
 

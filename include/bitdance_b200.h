@@ -16,9 +16,8 @@
  *       codes  [N/128][K/128][128 rows][64 bytes]   (same bytes, regrouped)
  *       scales [N/128][K/128][128 rows][8 bytes]
  *   MXFP6 activations A (bd_pack_a produces both from natural codes and scales):
- *       codes  (M, K) u8: every 16 consecutive K-elements occupy 16 bytes, the first 12
- *              holding the 16 six-bit E2M3 codes packed little-endian (code i at bits
- *              6i..6i+5), the last 4 bytes padding. This is the tensor-core operand image.
+ *       codes  (M, K) u8: one E2M3 code per byte (bits 0..5; bits 6..7 are ignored), the
+ *              byte image the tensor core takes from tensor memory.
  *       scales [K/128][Mp4][4] E8M0 bytes, Mp4 = M rounded up to a multiple of 4.
  *   MXFP6 codes in "natural" form (transcode output, bd_pack_a input): one E2M3 code per
  *       byte in bits [5:0] (sign<<5 | exp<<3 | mantissa); E8M0 = exponent + 127.
