@@ -170,7 +170,7 @@ def run_reference(args, rank, world):
     for _ in range(max(1, args.warmup)):
         cpu_reference_run(seconds=0.5)
     for _ in range(args.steps):
-        v, cores, sample = cpu_reference_run(seconds=max(1.0, args.cpu_seconds / max(1, args.steps)))
+        v, cores, sample = cpu_reference_run(seconds=max(0.25, args.cpu_seconds / max(1, args.steps)))
         vals.append(v)
     value = statistics.median(vals)
     line = {
@@ -524,7 +524,7 @@ def main():
         import torch
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group(
-            "nccl", timeout=datetime.timedelta(seconds=300),
+            "nccl", timeout=datetime.timedelta(seconds=120),
             device_id=torch.device("cuda", local_rank))
     try:
         if args.impl == "reference":
