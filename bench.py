@@ -412,9 +412,10 @@ def prefill_bench(torch, ops, dev, g, peaks):
 
 
 def run_case(args):
-    """One kernel shape, repeated: `--case gemm` (a single W4A6 GEMM) or `--case transcode`
-    (the standalone NVFP4 -> MXFP6 transcode of config 5). Prints its own JSON line; used for
-    Nsight Compute captures of one launch."""
+    """One kernel shape, repeated: `--case gemm` (a single W4A6 GEMM), `--case transcode`
+    (the standalone NVFP4 -> MXFP6 transcode of config 5) or `--case quantize` (the MXFP6
+    activation quantiser). Prints its own JSON line; used for Nsight Compute captures of one
+    launch."""
     import torch
     import bitdance_b200 as bd
     from bitdance_b200 import ops
@@ -456,6 +457,24 @@ def run_case(args):
         calls = args.steps
         work = {"M": M, "N": N, "K": K, "split_k": split, "overlap": ov, "rotating_weights": reps,
                 "weight_bytes": weight_bytes(N, K), "flops": 2 * M * N * K}
+    elif args.case == "quantize":
+        # fp32/bf16 activations -> GEMM-ready MXFP6 (codes + tiled scales) in one launch per
+        # call; the calls are captured in one CUDA graph (device time)
+        M, K = args.M, args.K
+        xdt = torch.bfloat16 if args.xdtype == "bf16" else torch.float32
+        x = torch.randn((M, K), device=dev, generator=g).to(xdt)
+        stream = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(stream):
+            ops.quantize_activations(x, stream=stream)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(args.steps):
+                ops.quantize_activations(x, stream=stream)
+        fn = graph.replay  # noqa: E731
+        calls = args.steps
+        work = {"M": M, "K": K, "x_dtype": args.xdtype,
+                "bytes": M * K * (x.element_size() + 1) + M * K // 32}
     else:
         nblk = args.nblk
         codes = torch.randint(0, 256, (nblk * 16,), dtype=torch.uint8, device=dev, generator=g)
@@ -467,12 +486,12 @@ def run_case(args):
         calls = 1
         work = {"nblk32": nblk, "bytes": nblk * (16 + 2 + 32 + 1)}
     with torch.cuda.stream(stream):
-        for _ in range(max(3, args.warmup if args.case != "gemm" else 3)):
+        for _ in range(max(3, args.warmup if args.case not in ("gemm", "quantize") else 3)):
             fn()
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    reps_t = 3 if args.case == "gemm" else args.steps
+    reps_t = 3 if args.case in ("gemm", "quantize") else args.steps
     with torch.cuda.stream(stream):
         t0.record(stream)
         for _ in range(reps_t):
@@ -494,7 +513,7 @@ def run_case(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", choices=["gemm", "transcode"], default=None,
+    ap.add_argument("--case", choices=["gemm", "transcode", "quantize"], default=None,
                     help="time one kernel shape instead of the benchmark step")
     ap.add_argument("--M", type=int, default=16)
     ap.add_argument("--N", type=int, default=14336)
@@ -503,6 +522,8 @@ def main():
     ap.add_argument("--overlap", type=int, default=1,
                     help="--case gemm: launch with programmatic serialisation (weights static)")
     ap.add_argument("--nblk", type=int, default=1 << 26)
+    ap.add_argument("--xdtype", choices=["bf16", "f32"], default="bf16",
+                    help="activation dtype of --case quantize")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)

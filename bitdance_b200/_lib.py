@@ -26,6 +26,8 @@ BD_OUT_BF16, BD_OUT_F16, BD_OUT_F32 = 0, 1, 2
 BD_EPI_NONE, BD_EPI_BIAS, BD_EPI_BIAS_RELU, BD_EPI_BIAS_SILU, BD_EPI_BIAS_GELU = 0, 1, 2, 3, 4
 BD_SPLIT_REDUCE, BD_SPLIT_PLANES, BD_SPLIT_ATOMIC = 0, 1, 2
 BD_GEMM_OVERLAP_PREV, BD_GEMM_WEIGHTS_STATIC = 1, 2
+BD_IN_F32, BD_IN_BF16 = 0, 1
+BD_DEVERR_WAIT_MASK, BD_DEVERR_WAIT_TMA, BD_DEVERR_NONFINITE = 0x1F, 0x01, 0x20
 
 # name -> (restype, argtypes); mirrors include/bitdance_b200.h
 _P = ctypes.c_void_p
@@ -37,9 +39,11 @@ SIGNATURES = {
     "bd_version": (_I, []),
     "bd_status_string": (ctypes.c_char_p, [_I]),
     "bd_device_error": (_I, [ctypes.POINTER(ctypes.c_uint32), _I]),
+    "bd_selftest_bounded_wait": (_I, [_I64, _P]),
     "bd_transcode_nvfp4_to_mxfp6": (_I, [_P, _P, _P, _P, _I64, _I, _P]),
     "bd_pack_b": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "bd_pack_a": (_I, [_P, _P, _P, _P, _I, _I, _P]),
+    "bd_quantize_a_mxfp6": (_I, [_P, _I, _P, _P, _P, _I, _I, _P]),
     "bd_query_workspace": (_SZ, [_I, _I, _I, _I, _I]),
     "bd_w4a6_gemm": (_I, [_P, _P, _P, _P, _P, _F, _P, _I, _I, _I, _I, _I, _I, _I, _P, _SZ, _P]),
     "bd_w4a6_gemm_ex": (_I, [_P, _P, _P, _P, _P, _F, _P, _I, _I, _I, _I, _I, _I, _I, _P, _SZ,

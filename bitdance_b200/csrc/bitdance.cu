@@ -59,6 +59,30 @@ int device_info(DeviceInfo** out) {
   return d.is_sm100 ? BD_OK : BD_ERR_ARCH;
 }
 
+// Diagnostic of the bounded waits: warp 0 waits on an mbarrier that nothing arrives at, with
+// a limit of `limit` cycles, and so records kErrWaitTma and raises the abort flag; warp 1 waits
+// on another such barrier with the GEMM's default limit and must leave through that flag.
+// The same mbar_wait as the GEMM's roles; it ends with a status, not a hung context.
+__global__ void wait_selftest_kernel(uint32_t* err, unsigned long long limit) {
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ uint32_t abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bars[0]), 1);
+    mbar_init(smem_u32(&bars[1]), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    if (warp == 0)
+      mbar_wait(smem_u32(&bars[0]), 0, err, kErrWaitTma, &abort_flag, limit);
+    else
+      mbar_wait(smem_u32(&bars[1]), 0, err, kErrWaitOperand, &abort_flag);
+  }
+  __syncwarp();
+}
+
 // Scratch of bd_w4a6_gemm_noalloc: the stream-K partial slots and per-tile counters of one
 // call live in this file-scope array instead of a caller-provided workspace, so that entry
 // point performs no device allocation. 16 MiB holds the stream-K scratch of every problem
@@ -239,6 +263,17 @@ int bd_device_error(uint32_t* word, int clear) {
   return BD_OK;
 }
 
+int bd_selftest_bounded_wait(int64_t limit_cycles, bd_stream_t stream) {
+  if (limit_cycles < 1000 || static_cast<unsigned long long>(limit_cycles) > kWaitLimitCycles)
+    return BD_ERR_INVALID_ARG;
+  DeviceInfo* d = nullptr;
+  int st = device_info(&d);
+  if (st != BD_OK) return st;
+  wait_selftest_kernel<<<1, 64, 0, as_stream(stream)>>>(
+      d->err, static_cast<unsigned long long>(limit_cycles));
+  return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
+}
+
 int bd_transcode_nvfp4_to_mxfp6(const uint8_t* codes, const uint8_t* scales, uint8_t* e2m3_out,
                                 uint8_t* e8m0_out, int64_t nblk32, int scale_block,
                                 bd_stream_t stream) {
@@ -296,6 +331,30 @@ int bd_pack_a(const uint8_t* codes, const uint8_t* e8m0, uint8_t* a_packed, uint
   const int64_t words = static_cast<int64_t>(K / 128) * Mp4;
   pack_a_scales_kernel<<<grid_for(words, 256, d), 256, 0, as_stream(stream)>>>(e8m0, scales_tiled,
                                                                                 M, Mp4, K);
+  return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
+}
+
+int bd_quantize_a_mxfp6(const void* x, int x_dtype, uint8_t* codes, uint8_t* e8m0,
+                        uint8_t* scales_tiled, int M, int K, bd_stream_t stream) {
+  if (x_dtype != BD_IN_F32 && x_dtype != BD_IN_BF16) return BD_ERR_INVALID_ARG;
+  if (!x || !codes || (!e8m0 && !scales_tiled)) return BD_ERR_INVALID_ARG;
+  if (M <= 0 || K <= 0 || K % 32 || (scales_tiled && K % 128)) return BD_ERR_SHAPE;
+  if (M > (1 << 30) / 4 || K > (1 << 24)) return BD_ERR_SHAPE;
+  if (!aligned(x, 16) || !aligned(codes, 16) || (scales_tiled && !aligned(scales_tiled, 4)))
+    return BD_ERR_ALIGNMENT;
+  DeviceInfo* d = nullptr;
+  int st = device_info(&d);
+  if (st != BD_OK) return st;
+  const int elems_per_vec = x_dtype == BD_IN_BF16 ? 8 : 4;
+  const int64_t nvec = static_cast<int64_t>(M) * K / elems_per_vec;
+  const int grid = grid_for((nvec + 3) / 4, 256, d);  // 4 vectors per lane per step
+  const int Mp4 = (M + 3) / 4 * 4;
+  if (x_dtype == BD_IN_BF16)
+    quantize_a_kernel<true><<<grid, 256, 0, as_stream(stream)>>>(
+        static_cast<const uint4*>(x), codes, e8m0, scales_tiled, M, K, Mp4, d->err);
+  else
+    quantize_a_kernel<false><<<grid, 256, 0, as_stream(stream)>>>(
+        static_cast<const uint4*>(x), codes, e8m0, scales_tiled, M, K, Mp4, d->err);
   return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
 }
 

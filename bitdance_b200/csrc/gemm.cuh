@@ -594,8 +594,12 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
             q[r][c] = *reinterpret_cast<const uint4*>(st + code_row[r] + ((c ^ sw[r]) << 4));
           sc[r] = *reinterpret_cast<const uint2*>(st + scale_off[r]);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&ctl.wempty[ws]));
+        // The weight stage is released only after the B rows computed from it are stored
+        // (below), never straight after the loads: the stores depend on every loaded word, so
+        // the stage cannot be refilled while a load of it is still outstanding. Releasing it
+        // right after the loads let the next fill of the stage land before some lanes' loads
+        // were performed when the bempty wait stalled (segment boundaries of long stream-K
+        // schedules), and those rows were converted from the chunk four places later.
         if (!mbar_wait(smem_u32(&ctl.bempty[bs]), bph ^ 1u, p.err, kErrWaitMma, abort_flag))
           break;
         const uint32_t bt = smem_u32(smem + Cfg::oB + bs * Cfg::kBStage);
@@ -623,7 +627,10 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         }
         fence_proxy_async_smem();  // the tensor core reads the B tile through the async proxy
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&ctl.sfready[bs]));
+        if (lane == 0) {
+          mbar_arrive(smem_u32(&ctl.wempty[ws]));
+          mbar_arrive(smem_u32(&ctl.sfready[bs]));
+        }
       }
     }
     // the fix-up of the tile of this CTA's last segment, when this CTA finishes it, is shared

@@ -19,6 +19,7 @@ enum : uint32_t {
   kErrWaitEmpty = 1u << 2,   // producer gave up waiting for a free stage
   kErrWaitAccum = 1u << 3,   // epilogue gave up waiting for the accumulator
   kErrWaitMma = 1u << 4,     // transcode gave up waiting for the MMA to free a buffer
+  kErrNonFinite = 1u << 5,   // the activation quantiser saw a NaN or an infinity
   kErrShape = 1u << 8,       // the kernel saw a shape it does not support
 };
 
@@ -76,12 +77,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait on phase `parity`. On time-out ORs `code` into *err and *abort and
-// returns false. Also returns false early if another role already aborted. The hot path is
-// a tight try_wait loop (try_wait itself suspends the thread in hardware for a while); the
-// abort flag and the cycle counter are looked at only every 1024 tries.
+// Bounded wait on phase `parity`. After `limit` SM cycles ORs `code` into *err, sets
+// *abort_flag and returns false. Also returns false early if another role already aborted.
+// The hot path is a tight try_wait loop (try_wait itself suspends the thread in hardware for
+// a while); the abort flag and the cycle counter are looked at only every 1024 tries.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t* err,
-                                          uint32_t code, volatile uint32_t* abort_flag) {
+                                          uint32_t code, volatile uint32_t* abort_flag,
+                                          unsigned long long limit = kWaitLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   uint32_t spins = 0;
@@ -89,7 +91,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_
     if (mbar_try_wait(bar, parity)) return true;
     if ((++spins & 1023u) == 0) {
       if (abort_flag != nullptr && *abort_flag) return false;
-      if (static_cast<unsigned long long>(clock64() - t0) > kWaitLimitCycles) {
+      if (static_cast<unsigned long long>(clock64() - t0) > limit) {
         if (err) atomicOr(err, code);
         if (abort_flag) *abort_flag = 1u;
         return false;

@@ -14,6 +14,7 @@
 // prmt turns four nibble selectors into four output bytes.
 #pragma once
 #include <cstdint>
+#include "sm100.cuh"
 #include "transcode_lut.cuh"
 
 namespace bd {
@@ -238,6 +239,138 @@ __global__ void pack_a_scales_kernel(const uint8_t* __restrict__ e8m0, uint8_t* 
     }
     reinterpret_cast<uint32_t*>(out)[i] = word;
   }
+}
+
+// ---------------------------------------------------------------------------------------
+// MXFP6 activation quantiser: fp32 / bf16 (M, K) -> E2M3 codes (M, K), one code per byte (the
+// GEMM's A layout as it stands) + E8M0 per 32-block, natural (M, K/32) and/or tiled for the GEMM
+// ([K/128][Mp4][4], padding rows 127).
+//
+// Rule (the reference's quantize(x, E8M0, E2M3), vector_quant_error.py:283-319): the block
+// exponent e is the smallest integer in [-40, 40] with 7.5 * 2^e >= amax (a zero block gets
+// e = 0); each element x / 2^e goes to the nearest E2M3 magnitude, an exact tie to the lower
+// one (argmin keeps the first minimum, :255-280); the sign bit is set for negative elements
+// whose magnitude code is not 0. With amax = m * 2^E (m in [1, 2)), 7.5 * 2^e = 1.875 * 2^(e+2),
+// so e = E - 2 + (m > 1.875). E2M3 magnitudes are k/8 below 2, 2 + k/4 below 4 and 4 + k/2
+// up to 7.5, so the nearest index with ties down is ceil(t - 0.5) of the scaled offset t.
+// Every step is exact in fp32 (power-of-two scaling; y - 2 and y - 4 by Sterbenz; t - 0.5 for
+// t >= 0.5 stays on t's grid, and t < 0.5 lands in [-0.5, 0) where the ceiling is 0 anyway),
+// so the codes equal the fp64 reference's.
+__device__ __forceinline__ uint32_t e2m3_code(float v, float inv_scale) {
+  const float y = fminf(fabsf(v) * inv_scale, 8.0f);
+  uint32_t idx;
+  if (y < 2.0f) {
+    idx = static_cast<uint32_t>(ceilf(y * 8.0f - 0.5f));
+  } else if (y < 4.0f) {
+    idx = 16u + static_cast<uint32_t>(ceilf((y - 2.0f) * 4.0f - 0.5f));
+  } else {
+    idx = min(31u, 24u + static_cast<uint32_t>(ceilf((y - 4.0f) * 2.0f - 0.5f)));
+  }
+  return idx | ((v < 0.0f && idx != 0u) ? 0x20u : 0u);
+}
+
+// Block exponent for a block amax >= 0 (see above), clamped to the E8M0 book's [-40, 40].
+__device__ __forceinline__ int mxfp6_block_exp(float amax) {
+  if (!(amax > 0.0f)) return 0;
+  const uint32_t bits = __float_as_uint(amax);
+  int E = static_cast<int>((bits >> 23) & 0xFFu) - 127;
+  uint32_t frac = bits & 0x7FFFFFu;
+  if (E == -127) {  // subnormal: normalise the fraction
+    const int sh = __clz(static_cast<int>(frac)) - 8;
+    frac = (frac << sh) & 0x7FFFFFu;
+    E = -126 - sh;
+  }
+  const int e = E - 2 + (frac > 0x700000u ? 1 : 0);
+  return max(-40, min(40, e));
+}
+
+// One warp takes 32 consecutive 16-byte vectors per step (coalesced); the lanes holding one
+// 32-block (8 lanes for fp32, 4 for bf16) reduce its amax with shuffles. kUnroll steps are
+// loaded before any is processed, to keep several loads in flight per lane.
+template <bool kBf16>
+__global__ void __launch_bounds__(256) quantize_a_kernel(const uint4* __restrict__ x,
+                                                         uint8_t* __restrict__ codes,
+                                                         uint8_t* __restrict__ e8m0,
+                                                         uint8_t* __restrict__ scales_tiled,
+                                                         int M, int K, int Mp4, uint32_t* err) {
+  constexpr int kEl = kBf16 ? 8 : 4;  // elements per 16-byte vector
+  constexpr int kVpb = 32 / kEl;      // vectors per 32-block
+  constexpr int kUnroll = 4;
+  const int64_t nvec = static_cast<int64_t>(M) * K / kEl;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int kb32 = K / 32;
+  bool bad = false;
+  for (int64_t base = warp * 32 * kUnroll; base < nvec; base += nwarps * 32 * kUnroll) {
+    uint4 w[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t v = base + u * 32 + lane;
+      w[u] = v < nvec ? ld_stream_u4(x + v) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t v = base + u * 32 + lane;
+      const uint32_t ws[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+      float f[kEl];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if constexpr (kBf16) {
+          f[2 * j] = __uint_as_float(ws[j] << 16);
+          f[2 * j + 1] = __uint_as_float(ws[j] & 0xFFFF0000u);
+        } else {
+          f[j] = __uint_as_float(ws[j]);
+        }
+      }
+      float amax = 0.0f;
+#pragma unroll
+      for (int j = 0; j < kEl; ++j) {
+        bad |= (__float_as_uint(f[j]) & 0x7F800000u) == 0x7F800000u;
+        amax = fmaxf(amax, fabsf(f[j]));
+      }
+#pragma unroll
+      for (int off = 1; off < kVpb; off <<= 1)
+        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
+      const int e = mxfp6_block_exp(amax);
+      const float inv_scale = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);  // 2^-e
+      if (v < nvec) {
+        if constexpr (kBf16) {
+          uint2 o;
+          o.x = e2m3_code(f[0], inv_scale) | (e2m3_code(f[1], inv_scale) << 8) |
+                (e2m3_code(f[2], inv_scale) << 16) | (e2m3_code(f[3], inv_scale) << 24);
+          o.y = e2m3_code(f[4], inv_scale) | (e2m3_code(f[5], inv_scale) << 8) |
+                (e2m3_code(f[6], inv_scale) << 16) | (e2m3_code(f[7], inv_scale) << 24);
+          reinterpret_cast<uint2*>(codes)[v] = o;
+        } else {
+          reinterpret_cast<uint32_t*>(codes)[v] =
+              e2m3_code(f[0], inv_scale) | (e2m3_code(f[1], inv_scale) << 8) |
+              (e2m3_code(f[2], inv_scale) << 16) | (e2m3_code(f[3], inv_scale) << 24);
+        }
+        if ((lane % kVpb) == 0) {
+          const int64_t blk = v / kVpb;
+          const uint8_t byte = static_cast<uint8_t>(e + 127);
+          if (e8m0 != nullptr) e8m0[blk] = byte;
+          if (scales_tiled != nullptr) {
+            const int64_t m = blk / kb32;
+            const int j = static_cast<int>(blk % kb32);
+            scales_tiled[((static_cast<int64_t>(j >> 2) * Mp4 + m) << 2) + (j & 3)] = byte;
+          }
+        }
+      }
+    }
+  }
+  if (scales_tiled != nullptr && Mp4 > M) {  // padding rows of the tiled scales
+    const int pad = Mp4 - M;
+    const int64_t total = static_cast<int64_t>(K / 128) * pad;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      const int64_t kc = i / pad;
+      const int m = M + static_cast<int>(i % pad);
+      reinterpret_cast<uint32_t*>(scales_tiled)[kc * Mp4 + m] = 0x7F7F7F7Fu;
+    }
+  }
+  if (bad) atomicOr(err, kErrNonFinite);
 }
 
 }  // namespace bd

@@ -79,7 +79,7 @@ class PackedWeights:
 @dataclass
 class PackedActivations:
     """MXFP6 activations in the GEMM operand layout."""
-    codes: torch.Tensor    # (M, K) u8, 12 packed bytes + 4 pad per 16 codes
+    codes: torch.Tensor    # (M, K) u8, one E2M3 code per byte (bits 0..5)
     scales: torch.Tensor   # [K/128][Mp4][4] E8M0 (flat)
     M: int
     K: int
@@ -108,6 +108,45 @@ def pack_activations(codes: torch.Tensor, e8m0: torch.Tensor, stream=None) -> Pa
     sc = torch.empty((K // 32) * mp4, dtype=torch.uint8, device=codes.device)
     call("bd_pack_a", _p(codes), _p(e8m0), _p(out), _p(sc), M, K, _stream(stream))
     return PackedActivations(out, sc, M, K)
+
+
+_IN = {torch.float32: _lib.BD_IN_F32, torch.bfloat16: _lib.BD_IN_BF16}
+
+
+def _check_x(x: torch.Tensor, k_mult: int):
+    if x.dim() != 2:
+        raise ValueError("x must be 2-D (M, K)")
+    if x.dtype not in _IN:
+        raise TypeError(f"x must be float32 or bfloat16, got {x.dtype}")
+    _need(x, x.dtype, "x")
+    M, K = x.shape
+    if K % k_mult:
+        raise ValueError(f"K must be a multiple of {k_mult}, got {K}")
+    return M, K
+
+
+def quantize_mxfp6(x: torch.Tensor, stream=None):
+    """Activations x (M, K) fp32/bf16 -> (E2M3 codes (M, K) u8, E8M0 (M, K/32) u8), the
+    reference's Direct-MXFP6 quantize(x, E8M0, E2M3) (vector_quant_error.py:305, :389) on the
+    GPU. NaN / Inf input sets BD_DEVERR_NONFINITE in the device error word (device_error())."""
+    M, K = _check_x(x, 32)
+    codes = torch.empty((M, K), dtype=torch.uint8, device=x.device)
+    e8m0 = torch.empty((M, K // 32), dtype=torch.uint8, device=x.device)
+    call("bd_quantize_a_mxfp6", _p(x), _IN[x.dtype], _p(codes), _p(e8m0), None, M, K,
+         _stream(stream))
+    return codes, e8m0
+
+
+def quantize_activations(x: torch.Tensor, stream=None) -> PackedActivations:
+    """Activations x (M, K) fp32/bf16 -> PackedActivations in one launch: the quantiser writes
+    the codes (already the GEMM's layout) and the tiled E8M0 scales directly. K % 128 == 0."""
+    M, K = _check_x(x, 128)
+    mp4 = (M + 3) // 4 * 4
+    codes = torch.empty((M, K), dtype=torch.uint8, device=x.device)
+    sc = torch.empty((K // 32) * mp4, dtype=torch.uint8, device=x.device)
+    call("bd_quantize_a_mxfp6", _p(x), _IN[x.dtype], _p(codes), None, _p(sc), M, K,
+         _stream(stream))
+    return PackedActivations(codes, sc, M, K)
 
 
 def query_workspace(M: int, N: int, K: int, split_k: int = 0, split_mode: str = "reduce") -> int:
@@ -213,7 +252,17 @@ def w4a6_gemm_noalloc(acts: PackedActivations, weights: PackedWeights, out: torc
 
 
 def device_error(clear: bool = True) -> int:
-    """Error word set by kernels whose bounded waits ran out (0 = none)."""
+    """Error word set by the library's kernels (0 = none): bits 0..4 a bounded wait of the
+    GEMM ran out, BD_DEVERR_NONFINITE (0x20) the quantiser saw NaN / Inf."""
     w = ctypes.c_uint32(0)
     call("bd_device_error", ctypes.byref(w), 1 if clear else 0)
     return int(w.value)
+
+
+def selftest_bounded_wait(limit_cycles: int = 2_000_000, stream=None) -> int:
+    """Run the bounded-wait diagnostic kernel (bd_selftest_bounded_wait) and return the device
+    error word it leaves, clearing it: BD_DEVERR_WAIT_TMA when the waits behave."""
+    if device_error(clear=True) != 0:
+        raise RuntimeError("device error word already set before the self-test")
+    call("bd_selftest_bounded_wait", int(limit_cycles), _stream(stream))
+    return device_error(clear=True)

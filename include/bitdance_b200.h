@@ -73,10 +73,23 @@ int bd_version(void);
 /* Human-readable text of a status code. */
 const char* bd_status_string(int status);
 
+/* Bits of the device error word (bd_device_error). */
+#define BD_DEVERR_WAIT_MASK 0x1Fu  /* a bounded wait of the GEMM ran out (bits 0..4)     */
+#define BD_DEVERR_WAIT_TMA 0x01u   /*   ... a consumer's wait for a TMA stage            */
+#define BD_DEVERR_NONFINITE 0x20u  /* bd_quantize_a_mxfp6 saw a NaN or an infinity      */
+
 /* Reads (and, if clear != 0, resets) the error word that kernels of this library set on
- * the current device when a bounded wait runs out. Synchronises the device. Returns BD_OK
- * and stores the word (0 = no error) in *word. */
+ * the current device: a bounded wait that ran out, non-finite quantiser input. Synchronises
+ * the device. Returns BD_OK and stores the word (0 = no error) in *word. */
 int bd_device_error(uint32_t* word, int clear);
+
+/* Diagnostic of the bounded waits (no reference counterpart): one CTA whose first warp waits
+ * on an mbarrier that nothing arrives at, with a limit of limit_cycles SM cycles, while a
+ * second warp waits on another with the GEMM's default limit (about 2 s). The first wait runs
+ * out, sets BD_DEVERR_WAIT_TMA in the device error word and raises the CTA's abort flag; the
+ * second leaves through that flag. The kernel ends, the context stays usable, and the host
+ * reads the status with bd_device_error. 1000 <= limit_cycles <= 4e9. */
+int bd_selftest_bounded_wait(int64_t limit_cycles, bd_stream_t stream);
 
 /* NVFP4 -> MXFP6 transcode, global -> global, natural layouts.
  * nblk32 blocks of 32 elements: codes 16 B per block, scales 2 B per block (scale_block 16,
@@ -101,6 +114,25 @@ int bd_pack_b(const uint8_t* codes, const uint8_t* scales16, uint8_t* codes_tile
  * build_Afrag, kernel/hip/w4a6_tc_gemm_v31.hip:608-615). */
 int bd_pack_a(const uint8_t* codes, const uint8_t* e8m0, uint8_t* a_packed,
               uint8_t* scales_tiled, int M, int K, bd_stream_t stream);
+
+/* Input element types of bd_quantize_a_mxfp6. */
+#define BD_IN_F32 0
+#define BD_IN_BF16 1
+
+/* Activations x (M, K) row-major, fp32 or bf16 -> MXFP6: E2M3 codes (M, K), one per byte (bits
+ * 0..5; this is already the GEMM's `a` operand), and the E8M0 exponent of each 32-element
+ * block along K, written to e8m0 (natural (M, K/32) layout) and/or scales_tiled (the GEMM's
+ * `a_scales` layout of bd_pack_a, K/32 * Mp4 bytes, padding rows 127); either may be NULL,
+ * not both. K % 32 == 0 (K % 128 == 0 when scales_tiled is given); x and codes 16-byte
+ * aligned.
+ * Rule: the block exponent is the smallest e in [-40, 40] with 7.5 * 2^e >= max|x| (a zero
+ * block gets e = 0); each x / 2^e goes to the nearest E2M3 magnitude, ties to the lower; the
+ * sign bit is kept only on non-zero codes. Bit-identical to the reference's
+ * quantize(x, E8M0, E2M3) (vector_quant_error.py:283-319, via the Direct-MXFP6 path :389).
+ * The reference refuses NaN / Inf input (:215-252); here such input sets BD_DEVERR_NONFINITE
+ * in the device error word (bd_device_error) and the affected blocks' outputs are undefined. */
+int bd_quantize_a_mxfp6(const void* x, int x_dtype, uint8_t* codes, uint8_t* e8m0,
+                        uint8_t* scales_tiled, int M, int K, bd_stream_t stream);
 
 /* Bytes of workspace bd_w4a6_gemm needs on the current device for this problem.
  * split_k == 0 (stream-K, the default schedule): per-CTA fp32 partial slots plus one arrival

@@ -296,3 +296,25 @@ def test_repeated_calls_are_bitwise_identical(split_k):
         assert torch.equal(got, ref), f"call {i} differs"
     torch.cuda.synchronize()
     assert bd.device_error() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 14336, 4096), (1024, 4096, 4096)])
+def test_streamk_long_segments_full_token_tile(M, N, K):
+    """128-row token tiles under stream-K with 12..27 K chunks per CTA: most CTAs run the tail
+    of one tile, store its partial, then start the next tile while the weight ring is full.
+    Every call is checked against the oracle (a weight stage released before its reads were
+    performed showed up here as rows converted from a later chunk, on some calls only)."""
+    import bitdance_b200 as bd
+    a_codes, a_e8, b_packed, b_sc = random_operands(M, N, K, seed=M + 5)
+    C, Cabs = gold(a_codes, a_e8, b_packed, b_sc, 1.0)
+    acts = bd.pack_activations(dev(a_codes), dev(a_e8))
+    w = bd.pack_weights(dev(b_packed), dev(b_sc), 1.0)
+    ws = bd.Workspace()
+    first = None
+    for i in range(4):
+        got = bd.w4a6_gemm(acts, w, out_dtype=torch.float32, workspace=ws)
+        check(got, C, Cabs, torch.float32)
+        if first is None:
+            first = got.clone()
+        assert torch.equal(got, first), f"call {i} differs"
+    assert bd.device_error() == 0
