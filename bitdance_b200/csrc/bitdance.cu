@@ -3,6 +3,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdint>
 #include <cstring>
@@ -340,21 +341,51 @@ int bd_quantize_a_mxfp6(const void* x, int x_dtype, uint8_t* codes, uint8_t* e8m
   if (!x || !codes || (!e8m0 && !scales_tiled)) return BD_ERR_INVALID_ARG;
   if (M <= 0 || K <= 0 || K % 32 || (scales_tiled && K % 128)) return BD_ERR_SHAPE;
   if (M > (1 << 30) / 4 || K > (1 << 24)) return BD_ERR_SHAPE;
+  if (static_cast<int64_t>(M) * K >= (int64_t{1} << 36)) return BD_ERR_SHAPE;  // block ids in 31 bits
   if (!aligned(x, 16) || !aligned(codes, 16) || (scales_tiled && !aligned(scales_tiled, 4)))
     return BD_ERR_ALIGNMENT;
   DeviceInfo* d = nullptr;
   int st = device_info(&d);
   if (st != BD_OK) return st;
-  const int elems_per_vec = x_dtype == BD_IN_BF16 ? 8 : 4;
-  const int64_t nvec = static_cast<int64_t>(M) * K / elems_per_vec;
-  const int grid = grid_for((nvec + 3) / 4, 256, d);  // 4 vectors per lane per step
+  const bool bf16 = x_dtype == BD_IN_BF16;
+  const uint64_t nblk = static_cast<uint64_t>(M) * static_cast<uint64_t>(K / 32);
+  const uint32_t row_bytes = bf16 ? QuantCfg<true>::kRowBytes : QuantCfg<false>::kRowBytes;
+  // one 32-element block per row; the kernel's stages are boxes of kQRows rows
+  CUtensorMap map;
+  if (!make_map_2d(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, const_cast<void*>(x), row_bytes, nblk,
+                   row_bytes, row_bytes, kQRows,
+                   bf16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B))
+    return BD_ERR_CUDA;
+  const int smem = bf16 ? QuantCfg<true>::kSmemBytes : QuantCfg<false>::kSmemBytes;
+  const int per_sm = bf16 ? QuantCfg<true>::kCtasPerSm : QuantCfg<false>::kCtasPerSm;
+  {
+    static std::atomic<uint64_t> configured{0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = (1ull << (dev & 31)) << (bf16 ? 32 : 0);
+    if (!(configured.load() & bit)) {
+      const cudaError_t e =
+          bf16 ? cudaFuncSetAttribute(quantize_a_kernel<true>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
+               : cudaFuncSetAttribute(quantize_a_kernel<false>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return BD_ERR_CUDA;
+      configured.fetch_or(bit);
+    }
+  }
+  const int64_t stages = static_cast<int64_t>((nblk + kQRows - 1) / kQRows);
+  const int grid = static_cast<int>(
+      std::min<int64_t>(stages, static_cast<int64_t>(d->sm_count) * per_sm));
   const int Mp4 = (M + 3) / 4 * 4;
-  if (x_dtype == BD_IN_BF16)
-    quantize_a_kernel<true><<<grid, 256, 0, as_stream(stream)>>>(
-        static_cast<const uint4*>(x), codes, e8m0, scales_tiled, M, K, Mp4, d->err);
+  // floor(2^64 / (K / 128)) + 1: chunk -> row by a multiply-high in the kernel
+  const uint64_t nkt = static_cast<uint64_t>(K / 128 > 0 ? K / 128 : 1);
+  const uint64_t nkt_magic = nkt > 1 ? ~0ull / nkt + 1 : 0;
+  if (bf16)
+    quantize_a_kernel<true><<<grid, kQThreads, smem, as_stream(stream)>>>(
+        map, codes, e8m0, scales_tiled, M, K, Mp4, nkt_magic, d->err);
   else
-    quantize_a_kernel<false><<<grid, 256, 0, as_stream(stream)>>>(
-        static_cast<const uint4*>(x), codes, e8m0, scales_tiled, M, K, Mp4, d->err);
+    quantize_a_kernel<false><<<grid, kQThreads, smem, as_stream(stream)>>>(
+        map, codes, e8m0, scales_tiled, M, K, Mp4, nkt_magic, d->err);
   return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
 }
 

@@ -250,127 +250,252 @@ __global__ void pack_a_scales_kernel(const uint8_t* __restrict__ e8m0, uint8_t* 
 // exponent e is the smallest integer in [-40, 40] with 7.5 * 2^e >= amax (a zero block gets
 // e = 0); each element x / 2^e goes to the nearest E2M3 magnitude, an exact tie to the lower
 // one (argmin keeps the first minimum, :255-280); the sign bit is set for negative elements
-// whose magnitude code is not 0. With amax = m * 2^E (m in [1, 2)), 7.5 * 2^e = 1.875 * 2^(e+2),
-// so e = E - 2 + (m > 1.875). E2M3 magnitudes are k/8 below 2, 2 + k/4 below 4 and 4 + k/2
-// up to 7.5, so the nearest index with ties down is ceil(t - 0.5) of the scaled offset t.
-// Every step is exact in fp32 (power-of-two scaling; y - 2 and y - 4 by Sterbenz; t - 0.5 for
-// t >= 0.5 stays on t's grid, and t < 0.5 lands in [-0.5, 0) where the ceiling is 0 anyway),
-// so the codes equal the fp64 reference's.
-__device__ __forceinline__ uint32_t e2m3_code(float v, float inv_scale) {
-  const float y = fminf(fabsf(v) * inv_scale, 8.0f);
-  uint32_t idx;
-  if (y < 2.0f) {
-    idx = static_cast<uint32_t>(ceilf(y * 8.0f - 0.5f));
-  } else if (y < 4.0f) {
-    idx = 16u + static_cast<uint32_t>(ceilf((y - 2.0f) * 4.0f - 0.5f));
-  } else {
-    idx = min(31u, 24u + static_cast<uint32_t>(ceilf((y - 4.0f) * 2.0f - 0.5f)));
-  }
-  return idx | ((v < 0.0f && idx != 0u) ? 0x20u : 0u);
+// whose magnitude code is not 0.
+//
+// Block exponent: with amax = m * 2^E (m in [1, 2)), 7.5 * 2^e = 1.875 * 2^(e+2), so
+// e = E - 2 + (m > 1.875); every amax below 2^-38 (subnormals included) clamps to -40.
+//
+// Element code, integer arithmetic on float bits (no conversions): for y = |x| / 2^e >= 1 the
+// E2M3 index is (exponent field - 126) * 8 + top three mantissa bits, rounded up when the 20
+// bits below them are strictly above half -- adding 0x7FFFF carries into bit 20 exactly then,
+// and a carry out of the mantissa moves to the next binade as the index does; so
+// idx = ((bits(y) + 0x7FFFF) >> 20) - 1008, capped at 31. For y < 1 (E2M3 subnormals, step 1/8)
+// the same formula applied to z = (y + 1) / 2 in [0.5, 1) gives round-half-down(8 y): z's
+// mantissa is y's binary expansion, and rounding z UP to float keeps the "strictly above half"
+// decision (a truncated remainder r with lost low bits is above half exactly when r >= half,
+// exactly when r + 1 ulp > half). z <= y for y >= 1 and z > y for y < 1, so max(y, z) picks
+// the right operand with no compare. y = |x| * 2^-e is exact (an exponent shift; values that
+// leave the normal range are far below 1/16 and map to code 0 either way).
+__device__ __forceinline__ uint32_t e2m3_mag(float v, float inv_scale) {
+  const float y = fabsf(v) * inv_scale;
+  const float z = __fmaf_ru(y, 0.5f, 0.5f);
+  const uint32_t t = __float_as_uint(fmaxf(y, z));
+  return min((t + (0x7FFFFu - (1008u << 20))) >> 20, 31u);
 }
 
-// Block exponent for a block amax >= 0 (see above), clamped to the E8M0 book's [-40, 40].
-__device__ __forceinline__ int mxfp6_block_exp(float amax) {
-  if (!(amax > 0.0f)) return 0;
-  const uint32_t bits = __float_as_uint(amax);
-  int E = static_cast<int>((bits >> 23) & 0xFFu) - 127;
-  uint32_t frac = bits & 0x7FFFFFu;
-  if (E == -127) {  // subnormal: normalise the fraction
-    const int sh = __clz(static_cast<int>(frac)) - 8;
-    frac = (frac << sh) & 0x7FFFFFu;
-    E = -126 - sh;
-  }
-  const int e = E - 2 + (frac > 0x700000u ? 1 : 0);
+// The same index left in bits 24..28 of the result (byte 3, so that byte permutes pack four of
+// them) for y <= 7.75, where (bits + 0x7FFFF - (1008 << 20)) mod 2^32 < 2^25: one multiply-add,
+// 16 * bits + 16 * (0x7FFFF - (1008 << 20)) mod 2^32. The block exponent keeps y <= 7.5 except
+// when it is clamped at 40; that case takes e2m3_mag.
+__device__ __forceinline__ uint32_t e2m3_mag_b3(float v, float inv_scale) {
+  const float y = fabsf(v) * inv_scale;
+  const float z = __fmaf_ru(y, 0.5f, 0.5f);
+  return __float_as_uint(fmaxf(y, z)) * 16u + 0x107FFFF0u;
+}
+
+// Byte 3 of each of four words -> one word (three byte permutes).
+__device__ __forceinline__ uint32_t gather_b3(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3) {
+  return prmt(prmt(x0, x1, 0x0073u), prmt(x2, x3, 0x7300u), 0x7610u);
+}
+
+// 4 magnitude codes (bytes, each <= 31) + 0xFF sign bytes of the negative elements -> 4 E2M3
+// codes; the sign (bit 5) is kept only on non-zero codes: for a byte b <= 31, b + 31 has bit 5
+// set exactly when b >= 1, with no carry between bytes.
+__device__ __forceinline__ uint32_t e2m3_word(uint32_t mags, uint32_t neg) {
+  return mags | ((mags + 0x1F1F1F1Fu) & neg & 0x20202020u);
+}
+
+__device__ __forceinline__ uint32_t pack4(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3) {
+  return c0 | (c1 << 8) | (c2 << 16) | (c3 << 24);
+}
+
+// max(a, b) that returns NaN when either is NaN.
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// Block exponent from the bits of the block amax (finite, sign cleared).
+__device__ __forceinline__ int mxfp6_block_exp(uint32_t amax_bits) {
+  if (amax_bits == 0u) return 0;
+  const int E = static_cast<int>(amax_bits >> 23) - 127;
+  const int e = E - 2 + ((amax_bits & 0x7FFFFFu) > 0x700000u ? 1 : 0);
   return max(-40, min(40, e));
 }
 
-// One warp takes 32 consecutive 16-byte vectors per step (coalesced); the lanes holding one
-// 32-block (8 lanes for fp32, 4 for bf16) reduce its amax with shuffles. kUnroll steps are
-// loaded before any is processed, to keep several loads in flight per lane.
+// Codes of 4 elements (fp32 values) with the block's 2^-e; `clamp` for blocks whose exponent
+// was clamped at 40 (elements may exceed 7.5 there).
+__device__ __forceinline__ uint32_t e2m3_mags4(float f0, float f1, float f2, float f3, float inv,
+                                               bool clamp) {
+  if (!clamp)
+    return gather_b3(e2m3_mag_b3(f0, inv), e2m3_mag_b3(f1, inv), e2m3_mag_b3(f2, inv),
+                     e2m3_mag_b3(f3, inv));
+  return pack4(e2m3_mag(f0, inv), e2m3_mag(f1, inv), e2m3_mag(f2, inv), e2m3_mag(f3, inv));
+}
+
+// Stage geometry of the quantiser. One consumer lane owns one 32-element block per stage: a
+// CTA is kQConsumerWarps consumer warps (256 lanes) plus one producer warp whose lane 0 loads
+// stages of 256 blocks into a shared-memory ring with 2-D tensor copies (completion on
+// mbarrier tx-counts), so loads stay in flight while the consumers compute. A block is one
+// swizzled shared-memory row (64 bytes of bf16 with the 64-byte swizzle, 128 bytes of fp32
+// with the 128-byte swizzle): lane t reads 16-byte chunk c of row t at chunk c ^ swz(t), and
+// the eight lanes of each shared-memory phase then cover all 32 banks.
+constexpr int kQConsumerWarps = 8;
+constexpr int kQThreads = 32 * (kQConsumerWarps + 1);
+constexpr int kQRows = 32 * kQConsumerWarps;  // blocks per stage
+
 template <bool kBf16>
-__global__ void __launch_bounds__(256) quantize_a_kernel(const uint4* __restrict__ x,
-                                                         uint8_t* __restrict__ codes,
-                                                         uint8_t* __restrict__ e8m0,
-                                                         uint8_t* __restrict__ scales_tiled,
-                                                         int M, int K, int Mp4, uint32_t* err) {
-  constexpr int kEl = kBf16 ? 8 : 4;  // elements per 16-byte vector
-  constexpr int kVpb = 32 / kEl;      // vectors per 32-block
-  constexpr int kUnroll = 4;
-  const int64_t nvec = static_cast<int64_t>(M) * K / kEl;
-  const int lane = threadIdx.x & 31;
-  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-  const int kb32 = K / 32;
-  bool bad = false;
-  for (int64_t base = warp * 32 * kUnroll; base < nvec; base += nwarps * 32 * kUnroll) {
-    uint4 w[kUnroll];
+struct QuantCfg {
+  static constexpr int kRowBytes = kBf16 ? 64 : 128;
+  static constexpr int kChunks = kRowBytes / 16;
+  static constexpr int kStageBytes = kQRows * kRowBytes;  // 16 KB / 32 KB
+  static constexpr int kStages = kBf16 ? 4 : 3;
+  static constexpr int kCtasPerSm = kBf16 ? 3 : 2;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024;  // + alignment slack
+  // chunk index bits XORed by the swizzle: address bits [5:4] ^= [8:7] (64-byte mode),
+  // [6:4] ^= [9:7] (128-byte mode), with rows of kRowBytes from a 1 KB aligned base
+  __device__ static __forceinline__ int swz(int row) { return kBf16 ? (row >> 1) & 3 : row & 7; }
+};
+
+// Quantise the 32-block in chunks q[] (its natural order): codes into 8 words o[], returns the
+// E8M0 byte; `bad` set when the block holds an Inf or NaN.
+template <bool kBf16>
+__device__ __forceinline__ uint32_t quantize_block(const uint4 (&q)[QuantCfg<kBf16>::kChunks],
+                                                   uint32_t (&o)[8], bool& bad) {
+  constexpr int kC = QuantCfg<kBf16>::kChunks;
+  float am = 0.0f;
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int64_t v = base + u * 32 + lane;
-      w[u] = v < nvec ? ld_stream_u4(x + v) : make_uint4(0u, 0u, 0u, 0u);
-    }
+  for (int c = 0; c < kC; ++c) {
+    const uint32_t ws[4] = {q[c].x, q[c].y, q[c].z, q[c].w};
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int64_t v = base + u * 32 + lane;
-      const uint32_t ws[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
-      float f[kEl];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if constexpr (kBf16) {
-          f[2 * j] = __uint_as_float(ws[j] << 16);
-          f[2 * j + 1] = __uint_as_float(ws[j] & 0xFFFF0000u);
-        } else {
-          f[j] = __uint_as_float(ws[j]);
-        }
-      }
-      float amax = 0.0f;
-#pragma unroll
-      for (int j = 0; j < kEl; ++j) {
-        bad |= (__float_as_uint(f[j]) & 0x7F800000u) == 0x7F800000u;
-        amax = fmaxf(amax, fabsf(f[j]));
-      }
-#pragma unroll
-      for (int off = 1; off < kVpb; off <<= 1)
-        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
-      const int e = mxfp6_block_exp(amax);
-      const float inv_scale = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);  // 2^-e
-      if (v < nvec) {
-        if constexpr (kBf16) {
-          uint2 o;
-          o.x = e2m3_code(f[0], inv_scale) | (e2m3_code(f[1], inv_scale) << 8) |
-                (e2m3_code(f[2], inv_scale) << 16) | (e2m3_code(f[3], inv_scale) << 24);
-          o.y = e2m3_code(f[4], inv_scale) | (e2m3_code(f[5], inv_scale) << 8) |
-                (e2m3_code(f[6], inv_scale) << 16) | (e2m3_code(f[7], inv_scale) << 24);
-          reinterpret_cast<uint2*>(codes)[v] = o;
-        } else {
-          reinterpret_cast<uint32_t*>(codes)[v] =
-              e2m3_code(f[0], inv_scale) | (e2m3_code(f[1], inv_scale) << 8) |
-              (e2m3_code(f[2], inv_scale) << 16) | (e2m3_code(f[3], inv_scale) << 24);
-        }
-        if ((lane % kVpb) == 0) {
-          const int64_t blk = v / kVpb;
-          const uint8_t byte = static_cast<uint8_t>(e + 127);
-          if (e8m0 != nullptr) e8m0[blk] = byte;
-          if (scales_tiled != nullptr) {
-            const int64_t m = blk / kb32;
-            const int j = static_cast<int>(blk % kb32);
-            scales_tiled[((static_cast<int64_t>(j >> 2) * Mp4 + m) << 2) + (j & 3)] = byte;
-          }
-        }
+    for (int j = 0; j < 4; ++j) {
+      if constexpr (kBf16) {
+        am = fmax_nan(am, fabsf(__uint_as_float(ws[j] << 16)));
+        am = fmax_nan(am, fabsf(__uint_as_float(ws[j] & 0xFFFF0000u)));
+      } else {
+        am = fmax_nan(am, fabsf(__uint_as_float(ws[j])));
       }
     }
   }
-  if (scales_tiled != nullptr && Mp4 > M) {  // padding rows of the tiled scales
-    const int pad = Mp4 - M;
-    const int64_t total = static_cast<int64_t>(K / 128) * pad;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-      const int64_t kc = i / pad;
-      const int m = M + static_cast<int>(i % pad);
-      reinterpret_cast<uint32_t*>(scales_tiled)[kc * Mp4 + m] = 0x7F7F7F7Fu;
+  const uint32_t amax = __float_as_uint(am);
+  bad |= amax >= 0x7F800000u;  // an Inf or NaN in the block
+  const int e = mxfp6_block_exp(amax);
+  const float inv = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);  // 2^-e
+  const bool clamp = e == 40;
+#pragma unroll
+  for (int c = 0; c < kC; ++c) {
+    const uint32_t w0 = q[c].x, w1 = q[c].y, w2 = q[c].z, w3 = q[c].w;
+    if constexpr (kBf16) {
+      // 0xFF sign bytes: bits 15 and 31 of each input word, replicated over the byte (a prmt
+      // selector nibble with its top bit set copies the sign of the selected byte)
+      o[2 * c] = e2m3_word(
+          e2m3_mags4(__uint_as_float(w0 << 16), __uint_as_float(w0 & 0xFFFF0000u),
+                     __uint_as_float(w1 << 16), __uint_as_float(w1 & 0xFFFF0000u), inv, clamp),
+          prmt(w0, w1, 0xFDB9u));
+      o[2 * c + 1] = e2m3_word(
+          e2m3_mags4(__uint_as_float(w2 << 16), __uint_as_float(w2 & 0xFFFF0000u),
+                     __uint_as_float(w3 << 16), __uint_as_float(w3 & 0xFFFF0000u), inv, clamp),
+          prmt(w2, w3, 0xFDB9u));
+    } else {
+      o[c] = e2m3_word(e2m3_mags4(__uint_as_float(w0), __uint_as_float(w1), __uint_as_float(w2),
+                                  __uint_as_float(w3), inv, clamp),
+                       prmt(prmt(w0, w1, 0x00FBu), prmt(w2, w3, 0xFB00u), 0x7610u));
     }
   }
-  if (bad) atomicOr(err, kErrNonFinite);
+  return static_cast<uint32_t>(e + 127);
+}
+
+template <bool kBf16>
+__global__ void __launch_bounds__(kQThreads, QuantCfg<kBf16>::kCtasPerSm)
+    quantize_a_kernel(const __grid_constant__ CUtensorMap tm_x, uint8_t* __restrict__ codes,
+                      uint8_t* __restrict__ e8m0, uint8_t* __restrict__ scales_tiled, int M,
+                      int K, int Mp4, uint64_t nkt_magic, uint32_t* err) {
+  using Cfg = QuantCfg<kBf16>;
+  extern __shared__ __align__(1024) uint8_t qsm_raw[];
+  uint8_t* qsm = qsm_raw + ((1024u - (smem_u32(qsm_raw) & 1023u)) & 1023u);
+  __shared__ __align__(8) uint64_t full[Cfg::kStages], empty[Cfg::kStages];
+  __shared__ uint32_t abort_word;
+  volatile uint32_t* abort_flag = &abort_word;
+  const int64_t nblk = static_cast<int64_t>(M) * (K / 32);
+  const int64_t nstage = (nblk + kQRows - 1) / kQRows;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    abort_word = 0;
+    for (int s = 0; s < Cfg::kStages; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), kQConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (warp == kQConsumerWarps) {
+    // ---- producer: stages blockIdx.x, + gridDim.x, ... (rows of 256 blocks) into the ring;
+    // a partial last stage is zero-filled past the last block and still counts the full box
+    if (lane == 0) {
+      prefetch_tmap(&tm_x);
+      int64_t i = 0;
+      for (int64_t s = blockIdx.x; s < nstage; s += gridDim.x, ++i) {
+        const int slot = static_cast<int>(i % Cfg::kStages);
+        const uint32_t ph = static_cast<uint32_t>(i / Cfg::kStages) & 1u;
+        if (!mbar_wait(smem_u32(&empty[slot]), ph ^ 1u, err, kErrWaitEmpty, abort_flag)) break;
+        mbar_arrive_expect_tx(smem_u32(&full[slot]), Cfg::kStageBytes);
+        tma_load_2d(smem_u32(qsm + slot * Cfg::kStageBytes), &tm_x, 0,
+                    static_cast<int32_t>(s * kQRows), smem_u32(&full[slot]));
+      }
+      // every copy issued has landed before the CTA exits: the last phase of each slot used
+      for (int64_t j = (i > Cfg::kStages ? i - Cfg::kStages : 0); j < i; ++j)
+        mbar_wait(smem_u32(&full[j % Cfg::kStages]), static_cast<uint32_t>(j / Cfg::kStages) & 1u,
+                  err, kErrWaitTma, nullptr);
+    }
+  } else {
+    // ---- consumers: lane t of the CTA quantises block t of each stage
+    const int t = threadIdx.x;
+    const uint32_t nkt = static_cast<uint32_t>(K / 128);
+    const int swz = Cfg::swz(t);
+    bool bad = false;
+    int64_t i = 0;
+    for (int64_t s = blockIdx.x; s < nstage; s += gridDim.x, ++i) {
+      const int slot = static_cast<int>(i % Cfg::kStages);
+      const uint32_t ph = static_cast<uint32_t>(i / Cfg::kStages) & 1u;
+      if (!mbar_wait(smem_u32(&full[slot]), ph, err, kErrWaitTma, abort_flag)) break;
+      const uint8_t* row = qsm + slot * Cfg::kStageBytes + t * Cfg::kRowBytes;
+      uint4 q[Cfg::kChunks];
+#pragma unroll
+      for (int c = 0; c < Cfg::kChunks; ++c)
+        q[c] = *reinterpret_cast<const uint4*>(row + ((c ^ swz) << 4));
+      uint32_t o[8];
+      const uint32_t byte = quantize_block<kBf16>(q, o, bad);
+      const int64_t b = s * kQRows + t;
+      const bool valid = b < nblk;
+      if (valid) {
+        uint4* dst = reinterpret_cast<uint4*>(codes + b * 32);
+        dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+        dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+        if (e8m0 != nullptr) e8m0[b] = static_cast<uint8_t>(byte);
+      }
+      if (scales_tiled != nullptr) {
+        // blocks 4j..4j+3 (one 128-element chunk of a row, K % 128 == 0) sit on lanes 4j..4j+3
+        const uint32_t b1 = __shfl_down_sync(0xFFFFFFFFu, byte, 1);
+        const uint32_t b2 = __shfl_down_sync(0xFFFFFFFFu, byte, 2);
+        const uint32_t b3 = __shfl_down_sync(0xFFFFFFFFu, byte, 3);
+        if ((lane & 3) == 0 && valid) {
+          // chunk -> (row, chunk in row): chunk < 2^31 and nkt < 2^17, so the high half of
+          // chunk * (floor(2^64 / nkt) + 1) is the exact quotient (nkt = 1 has no 64-bit magic)
+          const uint32_t chunk = static_cast<uint32_t>(b >> 2);
+          const uint32_t m =
+              nkt == 1u ? chunk : static_cast<uint32_t>(__umul64hi(chunk, nkt_magic));
+          const uint32_t kc = chunk - m * nkt;
+          reinterpret_cast<uint32_t*>(scales_tiled)[static_cast<int64_t>(kc) * Mp4 + m] =
+              pack4(byte, b1, b2, b3);
+        }
+      }
+      // the stage is released after the codes computed from it are stored
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&empty[slot]));
+    }
+    if (scales_tiled != nullptr && Mp4 > M) {  // padding rows of the tiled scales
+      const int pad = Mp4 - M;
+      const int64_t ptotal = static_cast<int64_t>(K / 128) * pad;
+      for (int64_t u = static_cast<int64_t>(blockIdx.x) * kQRows + t; u < ptotal;
+           u += static_cast<int64_t>(gridDim.x) * kQRows) {
+        const int64_t kc = u / pad;
+        const int m = M + static_cast<int>(u % pad);
+        reinterpret_cast<uint32_t*>(scales_tiled)[kc * Mp4 + m] = 0x7F7F7F7Fu;
+      }
+    }
+    if (bad) atomicOr(err, kErrNonFinite);
+  }
 }
 
 }  // namespace bd

@@ -2,8 +2,9 @@
 quantize_a_mxfp6, the reference's Direct-MXFP6 quantize(x, E8M0, E2M3)
 (vector_quant_error.py:283-319 via :389).
 
-CPU: the kernel's fp32 formulation (block exponent from the amax bits, ceil(t - 0.5) per
-E2M3 segment) restated in numpy float32 equals the fp64 oracle on adversarial blocks (exact
+CPU: the kernel's formulation (block exponent from the integer amax of the float bits, the
+E2M3 index from float bits with a carry-based round-half-down) restated in numpy equals the
+fp64 oracle on adversarial blocks (exact
 ties, block maxima at exactly 7.5 * 2^e and one ulp either side, the [-40, 40] exponent clamp,
 subnormals, signed zeros); the C ABI rejects bad arguments. GPU: the kernel is bit-exact
 against the oracle for fp32 and bf16 input, its tiled scales equal bd_pack_a's, a GEMM fed
@@ -59,30 +60,24 @@ def adversarial_blocks(seed: int = 0, nrand: int = 512) -> np.ndarray:
 
 
 def kernel_rule(x: np.ndarray):
-    """The kernel's fp32 steps (quantize_a_kernel in transcode.cuh), restated in numpy float32
-    for a CPU check of the exactness argument. Test-side only."""
+    """The kernel's steps (quantize_a_kernel in transcode.cuh), restated in numpy for a CPU
+    check of the exactness argument: block exponent from the integer amax of |bits|, element
+    index ((bits(max(y, z)) + 0x7FFFF) >> 20) - 1008 capped at 31 with y = |x| * 2^-e (float32)
+    and z = (y + 1) / 2 rounded up to float32. Test-side only."""
     f = np.asarray(x, dtype=np.float32).reshape(-1, 32)
-    amax = np.max(np.abs(f), axis=1)
-    bits = amax.view(np.uint32).astype(np.int64)
-    E = ((bits >> 23) & 0xFF) - 127
-    frac = bits & 0x7FFFFF
-    sub = (E == -127) & (frac > 0)
-    if sub.any():
-        lead = np.floor(np.log2(frac[sub])).astype(np.int64)  # position of the leading bit
-        sh = 23 - lead
-        frac[sub] = (frac[sub] << sh) & 0x7FFFFF
-        E[sub] = -126 - sh
-    e = np.clip(E - 2 + (frac > 0x700000), -40, 40)
-    e = np.where(amax > 0, e, 0)
+    ab = f.view(np.uint32) & np.uint32(0x7FFFFFFF)
+    amax = ab.max(axis=1).astype(np.int64)
+    e = (amax >> 23) - 127 - 2 + ((amax & 0x7FFFFF) > 0x700000)
+    e = np.where(amax == 0, 0, np.clip(e, -40, 40))
     inv = np.exp2(-e.astype(np.float64)).astype(np.float32)[:, None]
-    y = np.minimum(np.abs(f) * inv, np.float32(8))
-    h, q, t = np.float32(0.5), np.float32(2), np.float32(4)
-    i0 = np.ceil(y * np.float32(8) - h)
-    i1 = 16 + np.ceil((y - q) * np.float32(4) - h)
-    i2 = np.minimum(31, 24 + np.ceil((y - t) * np.float32(2) - h))
-    idx = np.where(y < q, i0, np.where(y < t, i1, i2)).astype(np.int64)
-    sign = (f < 0) & (idx != 0)
-    codes = (idx | (sign.astype(np.int64) << 5)).astype(np.uint8)
+    y = np.abs(f) * inv                                   # float32 product, exact here
+    z64 = (y.astype(np.float64) + 1.0) / 2.0
+    z = z64.astype(np.float32)                            # nearest ...
+    z = np.where(z.astype(np.float64) < z64, np.nextafter(z, np.float32(np.inf)), z)  # ... up
+    t = np.maximum(y, z).view(np.uint32).astype(np.int64)
+    mag = np.minimum((t + 0x7FFFF - (1008 << 20)) >> 20, 31)
+    sign = (f < 0) & (mag != 0)
+    codes = (mag | (sign.astype(np.int64) << 5)).astype(np.uint8)
     return codes.reshape(x.shape), (e + 127).astype(np.uint8).reshape(x.shape[0], -1)
 
 
@@ -164,15 +159,15 @@ def test_gpu_bit_exact_random_shapes(M, K, dtype):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("M", [1, 6, 64])
-def test_gpu_tiled_scales_equal_pack_a(M):
+@pytest.mark.parametrize("M,K", [(1, 512), (6, 512), (64, 512), (5, 128), (300, 384)])
+def test_gpu_tiled_scales_equal_pack_a(M, K):
     """quantize_activations (one launch, tiled scales written directly) == pack_activations of
     the natural outputs, padding rows included."""
     import torch
     import bitdance_b200 as bd
     g = torch.Generator(device="cuda")
     g.manual_seed(M)
-    x = torch.randn((M, 512), generator=g, device="cuda", dtype=torch.bfloat16)
+    x = torch.randn((M, K), generator=g, device="cuda", dtype=torch.bfloat16)
     packed = bd.quantize_activations(x)
     ref = bd.pack_activations(*bd.quantize_mxfp6(x))
     assert torch.equal(packed.codes, ref.codes)
