@@ -14,6 +14,8 @@
 // prmt turns four nibble selectors into four output bytes.
 #pragma once
 #include <cstdint>
+#include <cuda_bf16.h>
+
 #include "sm100.cuh"
 #include "transcode_lut.cuh"
 
@@ -354,18 +356,27 @@ template <bool kBf16>
 __device__ __forceinline__ uint32_t quantize_block(const uint4 (&q)[QuantCfg<kBf16>::kChunks],
                                                    uint32_t (&o)[8], bool& bad) {
   constexpr int kC = QuantCfg<kBf16>::kChunks;
+  // block amax, NaN-propagating (an Inf or NaN anywhere makes it non-finite); bf16 pairs are
+  // compared two at a time
   float am = 0.0f;
+  if constexpr (kBf16) {
+    __nv_bfloat162 m2 = __habs2(*reinterpret_cast<const __nv_bfloat162*>(&q[0].x));
 #pragma unroll
-  for (int c = 0; c < kC; ++c) {
-    const uint32_t ws[4] = {q[c].x, q[c].y, q[c].z, q[c].w};
+    for (int c = 0; c < kC; ++c) {
+      const uint32_t ws[4] = {q[c].x, q[c].y, q[c].z, q[c].w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if constexpr (kBf16) {
-        am = fmax_nan(am, fabsf(__uint_as_float(ws[j] << 16)));
-        am = fmax_nan(am, fabsf(__uint_as_float(ws[j] & 0xFFFF0000u)));
-      } else {
-        am = fmax_nan(am, fabsf(__uint_as_float(ws[j])));
-      }
+      for (int j = 0; j < 4; ++j)
+        m2 = __hmax2_nan(m2, __habs2(*reinterpret_cast<const __nv_bfloat162*>(&ws[j])));
+    }
+    const uint32_t mb = *reinterpret_cast<const uint32_t*>(&m2);
+    am = fmax_nan(__uint_as_float(mb << 16), __uint_as_float(mb & 0xFFFF0000u));
+  } else {
+#pragma unroll
+    for (int c = 0; c < kC; ++c) {
+      am = fmax_nan(am, fabsf(__uint_as_float(q[c].x)));
+      am = fmax_nan(am, fabsf(__uint_as_float(q[c].y)));
+      am = fmax_nan(am, fabsf(__uint_as_float(q[c].z)));
+      am = fmax_nan(am, fabsf(__uint_as_float(q[c].w)));
     }
   }
   const uint32_t amax = __float_as_uint(am);
