@@ -413,8 +413,9 @@ def prefill_bench(torch, ops, dev, g, peaks):
 
 def run_case(args):
     """One kernel shape, repeated: `--case gemm` (a single W4A6 GEMM), `--case transcode`
-    (the standalone NVFP4 -> MXFP6 transcode of config 5) or `--case quantize` (the MXFP6
-    activation quantiser). Prints its own JSON line; used for Nsight Compute captures of one
+    (the standalone NVFP4 -> MXFP6 transcode of config 5), `--case quantize` (the MXFP6
+    activation quantiser) or `--case quantize_b` (the NVFP4 weight quantiser; bytes count the
+    two passes over the weights). Prints its own JSON line; used for Nsight Compute captures of one
     launch."""
     import torch
     import bitdance_b200 as bd
@@ -475,6 +476,24 @@ def run_case(args):
         calls = args.steps
         work = {"M": M, "K": K, "x_dtype": args.xdtype,
                 "bytes": M * K * (x.element_size() + 1) + M * K // 32}
+    elif args.case == "quantize_b":
+        # fp32/bf16 weights (N, K) -> NVFP4 codes + E4M3 scales + tensor scale (amax pass and
+        # quantise pass), captured in one CUDA graph
+        N, K = args.N, args.K
+        wdt = torch.bfloat16 if args.xdtype == "bf16" else torch.float32
+        w = (torch.randn((N, K), device=dev, generator=g) * 0.02).to(wdt)
+        stream = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(stream):
+            ops.quantize_nvfp4(w, stream=stream)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(args.steps):
+                ops.quantize_nvfp4(w, stream=stream)
+        fn = graph.replay  # noqa: E731
+        calls = args.steps
+        work = {"N": N, "K": K, "w_dtype": args.xdtype,
+                "bytes": N * K * (2 * w.element_size() + 0.5) + N * K // 16}
     else:
         nblk = args.nblk
         codes = torch.randint(0, 256, (nblk * 16,), dtype=torch.uint8, device=dev, generator=g)
@@ -486,12 +505,12 @@ def run_case(args):
         calls = 1
         work = {"nblk32": nblk, "bytes": nblk * (16 + 2 + 32 + 1)}
     with torch.cuda.stream(stream):
-        for _ in range(max(3, args.warmup if args.case not in ("gemm", "quantize") else 3)):
+        for _ in range(max(3, args.warmup if args.case not in ("gemm", "quantize", "quantize_b") else 3)):
             fn()
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    reps_t = 3 if args.case in ("gemm", "quantize") else args.steps
+    reps_t = 3 if args.case in ("gemm", "quantize", "quantize_b") else args.steps
     with torch.cuda.stream(stream):
         t0.record(stream)
         for _ in range(reps_t):
@@ -513,7 +532,8 @@ def run_case(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", choices=["gemm", "transcode", "quantize"], default=None,
+    ap.add_argument("--case", choices=["gemm", "transcode", "quantize", "quantize_b"],
+                    default=None,
                     help="time one kernel shape instead of the benchmark step")
     ap.add_argument("--M", type=int, default=16)
     ap.add_argument("--N", type=int, default=14336)
@@ -523,7 +543,7 @@ def main():
                     help="--case gemm: launch with programmatic serialisation (weights static)")
     ap.add_argument("--nblk", type=int, default=1 << 26)
     ap.add_argument("--xdtype", choices=["bf16", "f32"], default="bf16",
-                    help="activation dtype of --case quantize")
+                    help="input dtype of --case quantize / quantize_b")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)

@@ -7,6 +7,7 @@ is its Python host side. ``psg`` mirrors the reference operator ``compile_preshu
 from ._lib import BitdanceError, load  # noqa: F401
 from .ops import (PackedActivations, PackedWeights, Workspace, device_error,  # noqa: F401
                   pack_activations, pack_weights, quantize_activations, quantize_mxfp6,
-                  query_workspace, transcode, w4a6_gemm, w4a6_gemm_noalloc)
+                  quantize_nvfp4, quantize_weights, query_workspace, tensor_scale_of,
+                  transcode, w4a6_gemm, w4a6_gemm_noalloc)
 
 __version__ = "0.1.0"

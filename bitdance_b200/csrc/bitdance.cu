@@ -11,6 +11,7 @@
 
 #include "../../include/bitdance_b200.h"
 #include "gemm.cuh"
+#include "quantize_b.cuh"
 #include "sm100.cuh"
 #include "transcode.cuh"
 
@@ -386,6 +387,35 @@ int bd_quantize_a_mxfp6(const void* x, int x_dtype, uint8_t* codes, uint8_t* e8m
   else
     quantize_a_kernel<false><<<grid, kQThreads, smem, as_stream(stream)>>>(
         map, codes, e8m0, scales_tiled, M, K, Mp4, nkt_magic, d->err);
+  return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
+}
+
+int bd_quantize_b_nvfp4(const void* w, int w_dtype, uint8_t* codes, uint8_t* scales16,
+                        uint32_t* tstat, int N, int K, bd_stream_t stream) {
+  if (w_dtype != BD_IN_F32 && w_dtype != BD_IN_BF16) return BD_ERR_INVALID_ARG;
+  if (!w || !codes || !scales16 || !tstat) return BD_ERR_INVALID_ARG;
+  if (N <= 0 || K <= 0 || K % 16) return BD_ERR_SHAPE;
+  if (static_cast<int64_t>(N) * K >= (int64_t{1} << 38)) return BD_ERR_SHAPE;
+  if (!aligned(w, 16) || !aligned(codes, 8) || !aligned(tstat, 4)) return BD_ERR_ALIGNMENT;
+  DeviceInfo* d = nullptr;
+  int st = device_info(&d);
+  if (st != BD_OK) return st;
+  const bool bf16 = w_dtype == BD_IN_BF16;
+  const int64_t nblk = static_cast<int64_t>(N) * (K / 16);
+  const int64_t nvec = nblk * (bf16 ? 2 : 4);
+  cudaStream_t s = as_stream(stream);
+  if (cudaMemsetAsync(tstat, 0, 2 * sizeof(uint32_t), s) != cudaSuccess) return BD_ERR_CUDA;
+  const uint4* wv = static_cast<const uint4*>(w);
+  const uint8_t* wb = static_cast<const uint8_t*>(w);
+  if (bf16) {
+    weight_amax_kernel<true><<<grid_for(nvec, 256, d), 256, 0, s>>>(wv, nvec, tstat, d->err);
+    quantize_b_kernel<true><<<grid_for(nblk, 256, d), 256, 0, s>>>(wb, codes, scales16, nblk,
+                                                                    tstat);
+  } else {
+    weight_amax_kernel<false><<<grid_for(nvec, 256, d), 256, 0, s>>>(wv, nvec, tstat, d->err);
+    quantize_b_kernel<false><<<grid_for(nblk, 256, d), 256, 0, s>>>(wb, codes, scales16, nblk,
+                                                                     tstat);
+  }
   return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
 }
 

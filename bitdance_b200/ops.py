@@ -149,6 +149,40 @@ def quantize_activations(x: torch.Tensor, stream=None) -> PackedActivations:
     return PackedActivations(codes, sc, M, K)
 
 
+def quantize_nvfp4(w: torch.Tensor, stream=None):
+    """Weights w (N, K) fp32/bf16 on the GPU -> (codes (N, K/2) packed E2M1 nibbles,
+    scales16 (N, K/16) E4M3 bytes, tstat (2,) int32 device tensor: tstat[0] the fp32 tensor
+    scale's bits, tstat[1] the bits of amax(|w|)): the reference's two-level NVFP4 encode
+    (remote/quant_real_weights.py:273-287 + kernel/nvfp4_codec.py:34-63) on the GPU, K % 16 == 0.
+    NaN / Inf input sets BD_DEVERR_NONFINITE in the device error word."""
+    if w.dim() != 2:
+        raise ValueError("w must be 2-D (N, K)")
+    if w.dtype not in _IN:
+        raise TypeError(f"w must be float32 or bfloat16, got {w.dtype}")
+    _need(w, w.dtype, "w")
+    N, K = w.shape
+    if K % 16:
+        raise ValueError(f"K must be a multiple of 16, got {K}")
+    codes = torch.empty((N, K // 2), dtype=torch.uint8, device=w.device)
+    scales = torch.empty((N, K // 16), dtype=torch.uint8, device=w.device)
+    tstat = torch.empty(2, dtype=torch.int32, device=w.device)
+    call("bd_quantize_b_nvfp4", _p(w), _IN[w.dtype], _p(codes), _p(scales), _p(tstat), N, K,
+         _stream(stream))
+    return codes, scales, tstat
+
+
+def tensor_scale_of(tstat: torch.Tensor) -> float:
+    """The fp32 tensor scale held in tstat[0] (reads it back to the host)."""
+    return float(tstat[:1].view(torch.float32).item())
+
+
+def quantize_weights(w: torch.Tensor, stream=None) -> PackedWeights:
+    """Weights w (N, K) fp32/bf16 -> PackedWeights (NVFP4 quantised on the GPU, then tiled for
+    the GEMM). N % 128 == 0, K % 128 == 0. Reads the tensor scale back to the host once."""
+    codes, scales, tstat = quantize_nvfp4(w, stream)
+    return pack_weights(codes, scales, tensor_scale_of(tstat), stream)
+
+
 def query_workspace(M: int, N: int, K: int, split_k: int = 0, split_mode: str = "reduce") -> int:
     return int(_lib.load().bd_query_workspace(M, N, K, split_k, SPLIT_MODES[split_mode]))
 

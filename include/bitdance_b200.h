@@ -76,7 +76,7 @@ const char* bd_status_string(int status);
 /* Bits of the device error word (bd_device_error). */
 #define BD_DEVERR_WAIT_MASK 0x1Fu  /* a bounded wait of the GEMM ran out (bits 0..4)     */
 #define BD_DEVERR_WAIT_TMA 0x01u   /*   ... a consumer's wait for a TMA stage            */
-#define BD_DEVERR_NONFINITE 0x20u  /* bd_quantize_a_mxfp6 saw a NaN or an infinity      */
+#define BD_DEVERR_NONFINITE 0x20u  /* a quantiser saw a NaN or an infinity               */
 
 /* Reads (and, if clear != 0, resets) the error word that kernels of this library set on
  * the current device: a bounded wait that ran out, non-finite quantiser input. Synchronises
@@ -115,7 +115,7 @@ int bd_pack_b(const uint8_t* codes, const uint8_t* scales16, uint8_t* codes_tile
 int bd_pack_a(const uint8_t* codes, const uint8_t* e8m0, uint8_t* a_packed,
               uint8_t* scales_tiled, int M, int K, bd_stream_t stream);
 
-/* Input element types of bd_quantize_a_mxfp6. */
+/* Input element types of bd_quantize_a_mxfp6 and bd_quantize_b_nvfp4. */
 #define BD_IN_F32 0
 #define BD_IN_BF16 1
 
@@ -133,6 +133,20 @@ int bd_pack_a(const uint8_t* codes, const uint8_t* e8m0, uint8_t* a_packed,
  * in the device error word (bd_device_error) and the affected blocks' outputs are undefined. */
 int bd_quantize_a_mxfp6(const void* x, int x_dtype, uint8_t* codes, uint8_t* e8m0,
                         uint8_t* scales_tiled, int M, int K, bd_stream_t stream);
+
+/* Weights w (N, K) row-major, fp32 or bf16 -> NVFP4 with per-16 E4M3 scales and an fp32
+ * per-tensor scale, the natural layouts bd_pack_b takes: codes (N, K/2) E2M1 nibbles (element
+ * 2j in the low nibble of byte j), scales16 (N, K/16) E4M3 bytes. tstat is a device buffer of
+ * two 32-bit words: on return (stream order) tstat[0] holds the tensor scale s_t as a float and
+ * tstat[1] the bits of amax(|w|). K % 16 == 0; w 16-byte aligned, codes 8-byte aligned.
+ * Rule: s_t = float32(amax / 2688) (1.0 for an all-zero tensor), v = w / s_t in float32; per
+ * 16-block the smallest E4M3FN normal >= amax(|v|)/6 (448 at most, 1.0 for a zero block) and the
+ * nearest E2M1 magnitude of v / scale, ties to the lower, sign only on non-zero codes.
+ * Bit-identical to the reference's two-level NVFP4 encode (run_method,
+ * remote/quant_real_weights.py:273-287; encode_nvfp4, kernel/nvfp4_codec.py:34-63). NaN / Inf
+ * input sets BD_DEVERR_NONFINITE (the reference raises) and the outputs are undefined. */
+int bd_quantize_b_nvfp4(const void* w, int w_dtype, uint8_t* codes, uint8_t* scales16,
+                        uint32_t* tstat, int N, int K, bd_stream_t stream);
 
 /* Bytes of workspace bd_w4a6_gemm needs on the current device for this problem.
  * split_k == 0 (stream-K, the default schedule): per-CTA fp32 partial slots plus one arrival
