@@ -326,9 +326,12 @@ int bd_pack_a(const uint8_t* codes, const uint8_t* e8m0, uint8_t* a_packed, uint
   DeviceInfo* d = nullptr;
   int st = device_info(&d);
   if (st != BD_OK) return st;
+  // the natural codes are already the operand layout (the GEMM ignores bits 6..7): with
+  // a_packed == codes only the scales are re-laid out
   const int64_t nchunks = static_cast<int64_t>(M) * K / 16;
-  pack_a_codes_kernel<<<grid_for(nchunks, 256, d), 256, 0, as_stream(stream)>>>(codes, a_packed,
-                                                                                 nchunks);
+  if (a_packed != codes)
+    pack_a_codes_kernel<<<grid_for(nchunks, 256, d), 256, 0, as_stream(stream)>>>(codes, a_packed,
+                                                                                   nchunks);
   const int Mp4 = (M + 3) / 4 * 4;
   const int64_t words = static_cast<int64_t>(K / 128) * Mp4;
   pack_a_scales_kernel<<<grid_for(words, 256, d), 256, 0, as_stream(stream)>>>(e8m0, scales_tiled,

@@ -98,13 +98,16 @@ def pack_weights(codes: torch.Tensor, scales16: torch.Tensor, tensor_scale: floa
     return PackedWeights(tc, ts, float(tensor_scale), N, K)
 
 
-def pack_activations(codes: torch.Tensor, e8m0: torch.Tensor, stream=None) -> PackedActivations:
-    """codes (M, K) one E2M3 code per byte, e8m0 (M, K/32) -> PackedActivations."""
+def pack_activations(codes: torch.Tensor, e8m0: torch.Tensor, stream=None,
+                     inplace: bool = False) -> PackedActivations:
+    """codes (M, K) one E2M3 code per byte, e8m0 (M, K/32) -> PackedActivations. The codes are
+    already the operand layout; inplace=True uses `codes` itself as the operand (no copy, only
+    the scales are re-laid out), so later writes to `codes` change the operand."""
     M, K = codes.shape
     _need(codes, torch.uint8, "codes")
     _need(e8m0, torch.uint8, "e8m0", M * K // 32)
     mp4 = (M + 3) // 4 * 4
-    out = torch.empty((M, K), dtype=torch.uint8, device=codes.device)
+    out = codes if inplace else torch.empty((M, K), dtype=torch.uint8, device=codes.device)
     sc = torch.empty((K // 32) * mp4, dtype=torch.uint8, device=codes.device)
     call("bd_pack_a", _p(codes), _p(e8m0), _p(out), _p(sc), M, K, _stream(stream))
     return PackedActivations(out, sc, M, K)

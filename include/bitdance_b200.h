@@ -109,7 +109,9 @@ int bd_pack_b(const uint8_t* codes, const uint8_t* scales16, uint8_t* codes_tile
               uint8_t* scales_tiled, int N, int K, bd_stream_t stream);
 
 /* Natural MXFP6 A (one code per byte, (M, K/32) E8M0) -> GEMM operand layout. K % 128 == 0.
- * scales_tiled must hold K/32 * Mp4 bytes; padding rows are written as 127 (2^0).
+ * scales_tiled must hold K/32 * Mp4 bytes; padding rows are written as 127 (2^0). The codes are
+ * already in the operand layout: a_packed receives a copy with bits 6..7 cleared, and
+ * a_packed == codes is allowed (nothing is copied; only the scales are re-laid out).
  * Replaces the reference's A packing (pack6_block, kernel/verify_w4a6.py:55-59;
  * build_Afrag, kernel/hip/w4a6_tc_gemm_v31.hip:608-615). */
 int bd_pack_a(const uint8_t* codes, const uint8_t* e8m0, uint8_t* a_packed,

@@ -318,3 +318,20 @@ def test_streamk_long_segments_full_token_tile(M, N, K):
             first = got.clone()
         assert torch.equal(got, first), f"call {i} differs"
     assert bd.device_error() == 0
+
+
+def test_pack_activations_in_place_gives_the_same_gemm():
+    """pack_activations(..., inplace=True) uses the natural codes as the operand (only the scales
+    are re-laid out) and gives the same result as the copying form, also with bits 6..7 of the
+    code bytes set (the GEMM ignores them)."""
+    import bitdance_b200 as bd
+    M, N, K = 24, 512, 1024
+    a_codes, a_e8, b_packed, b_sc = random_operands(M, N, K, seed=41)
+    junk = (np.random.default_rng(1).integers(0, 4, a_codes.shape) << 6).astype(np.uint8)
+    w = bd.pack_weights(dev(b_packed), dev(b_sc), 1.0)
+    ref = bd.w4a6_gemm(bd.pack_activations(dev(a_codes), dev(a_e8)), w)
+    codes = dev(a_codes | junk)
+    packed = bd.pack_activations(codes, dev(a_e8), inplace=True)
+    assert packed.codes.data_ptr() == codes.data_ptr()
+    got = bd.w4a6_gemm(packed, w)
+    assert torch.equal(got, ref)
