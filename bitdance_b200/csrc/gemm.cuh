@@ -596,10 +596,12 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         }
         // The weight stage is released only after the B rows computed from it are stored
         // (below), never straight after the loads: the stores depend on every loaded word, so
-        // the stage cannot be refilled while a load of it is still outstanding. Releasing it
-        // right after the loads let the next fill of the stage land before some lanes' loads
-        // were performed when the bempty wait stalled (segment boundaries of long stream-K
-        // schedules), and those rows were converted from the chunk four places later.
+        // the stage cannot be refilled while a load of it is still outstanding. An arrive
+        // right after the loads (a release that orders this thread's stores, not its loads)
+        // let the next fill of the stage land before some loads were performed when the
+        // bempty wait stalled (segment boundaries of long stream-K schedules): those rows came
+        // out converted from the chunk four places later. Volatile loads did not prevent it;
+        // folding every loaded word into a value stored before the arrive did, at no gain.
         if (!mbar_wait(smem_u32(&ctl.bempty[bs]), bph ^ 1u, p.err, kErrWaitMma, abort_flag))
           break;
         const uint32_t bt = smem_u32(smem + Cfg::oB + bs * Cfg::kBStage);
