@@ -488,6 +488,34 @@ def run_case(args):
         calls = args.steps
         work = {"M": M, "N": N, "K": K, "split_k": split, "overlap": ov, "rotating_weights": reps,
                 "weight_bytes": weight_bytes(N, K), "flops": 2 * M * N * K}
+    elif args.case == "linear":
+        # raw bf16 activations -> on-device quantiser -> GEMM (w4a6_linear), over rotating
+        # weight matrices, captured in one CUDA graph
+        M, N, K = args.M, args.N, args.K
+        reps = max(2, -(-300_000_000 // weight_bytes(N, K)))
+        ws_list = [ops.pack_weights(torch.randint(0, 256, (N, K // 2), dtype=torch.uint8,
+                                                  device=dev, generator=g),
+                                    torch.randint(0x58, 0x7F, (N, K // 16), dtype=torch.uint8,
+                                                  device=dev, generator=g), 1.0)
+                   for _ in range(reps)]
+        x = torch.randn((M, K), device=dev, generator=g).to(torch.bfloat16)
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        wsp = ops.Workspace()
+        stream = torch.cuda.Stream(device=dev)
+
+        def body():
+            for i in range(args.steps):
+                ops.w4a6_linear(x, ws_list[i % reps], out=out, workspace=wsp, stream=stream)
+        with torch.cuda.stream(stream):
+            body()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            body()
+        fn = graph.replay  # noqa: E731
+        calls = args.steps
+        work = {"M": M, "N": N, "K": K, "rotating_weights": reps,
+                "weight_bytes": weight_bytes(N, K), "flops": 2 * M * N * K}
     elif args.case == "quantize":
         # fp32/bf16 activations -> GEMM-ready MXFP6 (codes + tiled scales) in one launch per
         # call; the calls are captured in one CUDA graph (device time)
@@ -535,12 +563,13 @@ def run_case(args):
         calls = 1
         work = {"nblk32": nblk, "bytes": nblk * (16 + 2 + 32 + 1)}
     with torch.cuda.stream(stream):
-        for _ in range(max(3, args.warmup if args.case not in ("gemm", "quantize", "quantize_b") else 3)):
+        for _ in range(max(3, args.warmup if args.case not in ("gemm", "linear", "quantize",
+                                                               "quantize_b") else 3)):
             fn()
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    reps_t = 3 if args.case in ("gemm", "quantize", "quantize_b") else args.steps
+    reps_t = 3 if args.case in ("gemm", "linear", "quantize", "quantize_b") else args.steps
     with torch.cuda.stream(stream):
         t0.record(stream)
         for _ in range(reps_t):
@@ -549,7 +578,7 @@ def run_case(args):
     torch.cuda.synchronize()
     us = t0.elapsed_time(t1) * 1e3 / (reps_t * calls)
     res = {"case": args.case, "us_per_call": us, **work}
-    if args.case == "gemm":
+    if args.case in ("gemm", "linear"):
         res["weight_gbs"] = work["weight_bytes"] / us / 1e3
         res["tflops"] = work["flops"] / us / 1e6
     else:
@@ -562,7 +591,7 @@ def run_case(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", choices=["gemm", "transcode", "quantize", "quantize_b"],
+    ap.add_argument("--case", choices=["gemm", "linear", "transcode", "quantize", "quantize_b"],
                     default=None,
                     help="time one kernel shape instead of the benchmark step")
     ap.add_argument("--M", type=int, default=16)

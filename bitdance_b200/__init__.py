@@ -8,6 +8,6 @@ from ._lib import BitdanceError, load  # noqa: F401
 from .ops import (PackedActivations, PackedWeights, Workspace, device_error,  # noqa: F401
                   pack_activations, pack_weights, quantize_activations, quantize_mxfp6,
                   quantize_nvfp4, quantize_weights, query_workspace, tensor_scale_of,
-                  transcode, w4a6_gemm, w4a6_gemm_noalloc)
+                  transcode, w4a6_gemm, w4a6_gemm_noalloc, w4a6_linear)
 
 __version__ = "0.1.0"

@@ -45,6 +45,7 @@ SIGNATURES = {
     "bd_pack_a": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "bd_quantize_a_mxfp6": (_I, [_P, _I, _P, _P, _P, _I, _I, _P]),
     "bd_quantize_b_nvfp4": (_I, [_P, _I, _P, _P, _P, _I, _I, _P]),
+    "bd_quantize_a_mxfp6_ex": (_I, [_P, _I, _P, _P, _P, _I, _I, ctypes.c_uint, _P]),
     "bd_query_workspace": (_SZ, [_I, _I, _I, _I, _I]),
     "bd_w4a6_gemm": (_I, [_P, _P, _P, _P, _P, _F, _P, _I, _I, _I, _I, _I, _I, _I, _P, _SZ, _P]),
     "bd_w4a6_gemm_ex": (_I, [_P, _P, _P, _P, _P, _F, _P, _I, _I, _I, _I, _I, _I, _I, _P, _SZ,

@@ -341,6 +341,13 @@ int bd_pack_a(const uint8_t* codes, const uint8_t* e8m0, uint8_t* a_packed, uint
 
 int bd_quantize_a_mxfp6(const void* x, int x_dtype, uint8_t* codes, uint8_t* e8m0,
                         uint8_t* scales_tiled, int M, int K, bd_stream_t stream) {
+  return bd_quantize_a_mxfp6_ex(x, x_dtype, codes, e8m0, scales_tiled, M, K, 0u, stream);
+}
+
+int bd_quantize_a_mxfp6_ex(const void* x, int x_dtype, uint8_t* codes, uint8_t* e8m0,
+                           uint8_t* scales_tiled, int M, int K, unsigned flags,
+                           bd_stream_t stream) {
+  if (flags & ~static_cast<unsigned>(BD_GEMM_OVERLAP_PREV)) return BD_ERR_INVALID_ARG;
   if (x_dtype != BD_IN_F32 && x_dtype != BD_IN_BF16) return BD_ERR_INVALID_ARG;
   if (!x || !codes || (!e8m0 && !scales_tiled)) return BD_ERR_INVALID_ARG;
   if (M <= 0 || K <= 0 || K % 32 || (scales_tiled && K % 128)) return BD_ERR_SHAPE;
@@ -384,12 +391,22 @@ int bd_quantize_a_mxfp6(const void* x, int x_dtype, uint8_t* codes, uint8_t* e8m
   // floor(2^64 / (K / 128)) + 1: chunk -> row by a multiply-high in the kernel
   const uint64_t nkt = static_cast<uint64_t>(K / 128 > 0 ? K / 128 : 1);
   const uint64_t nkt_magic = nkt > 1 ? ~0ull / nkt + 1 : 0;
-  if (bf16)
-    quantize_a_kernel<true><<<grid, kQThreads, smem, as_stream(stream)>>>(
-        map, codes, e8m0, scales_tiled, M, K, Mp4, nkt_magic, d->err);
-  else
-    quantize_a_kernel<false><<<grid, kQThreads, smem, as_stream(stream)>>>(
-        map, codes, e8m0, scales_tiled, M, K, Mp4, nkt_magic, d->err);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kQThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (flags & BD_GEMM_OVERLAP_PREV) ? 1 : 0;
+  const cudaError_t e =
+      bf16 ? cudaLaunchKernelEx(&cfg, quantize_a_kernel<true>, map, codes, e8m0, scales_tiled, M,
+                                K, Mp4, nkt_magic, d->err)
+           : cudaLaunchKernelEx(&cfg, quantize_a_kernel<false>, map, codes, e8m0, scales_tiled, M,
+                                K, Mp4, nkt_magic, d->err);
+  if (e != cudaSuccess) return BD_ERR_CUDA;
   return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
 }
 

@@ -430,6 +430,12 @@ __global__ void __launch_bounds__(kQThreads, QuantCfg<kBf16>::kCtasPerSm)
     fence_mbar_init();
   }
   __syncthreads();
+  // a kernel launched after this one with programmatic serialisation (the GEMM that consumes
+  // these codes) may be scheduled on free SMs now; it waits for this grid before reading them.
+  // When this grid was itself launched that way, x and the outputs belong to the previous grid
+  // until it completes (it may still be reading a recycled output buffer).
+  grid_dep_launch_dependents();
+  grid_dep_wait();
   if (warp == kQConsumerWarps) {
     // ---- producer: stages blockIdx.x, + gridDim.x, ... (rows of 256 blocks) into the ring;
     // a partial last stage is zero-filled past the last block and still counts the full box

@@ -140,15 +140,18 @@ def quantize_mxfp6(x: torch.Tensor, stream=None):
     return codes, e8m0
 
 
-def quantize_activations(x: torch.Tensor, stream=None) -> PackedActivations:
+def quantize_activations(x: torch.Tensor, stream=None,
+                         overlap_prev: bool = False) -> PackedActivations:
     """Activations x (M, K) fp32/bf16 -> PackedActivations in one launch: the quantiser writes
-    the codes (already the GEMM's layout) and the tiled E8M0 scales directly. K % 128 == 0."""
+    the codes (already the GEMM's layout) and the tiled E8M0 scales directly. K % 128 == 0.
+    overlap_prev: launched with programmatic serialisation (it waits for the previous kernel
+    on the stream before reading x or writing its outputs)."""
     M, K = _check_x(x, 128)
     mp4 = (M + 3) // 4 * 4
     codes = torch.empty((M, K), dtype=torch.uint8, device=x.device)
     sc = torch.empty((K // 32) * mp4, dtype=torch.uint8, device=x.device)
-    call("bd_quantize_a_mxfp6", _p(x), _IN[x.dtype], _p(codes), None, _p(sc), M, K,
-         _stream(stream))
+    call("bd_quantize_a_mxfp6_ex", _p(x), _IN[x.dtype], _p(codes), None, _p(sc), M, K,
+         _lib.BD_GEMM_OVERLAP_PREV if overlap_prev else 0, _stream(stream))
     return PackedActivations(codes, sc, M, K)
 
 
@@ -263,6 +266,19 @@ def w4a6_gemm(acts: PackedActivations, weights: PackedWeights,
          0 if workspace is None else workspace.numel() * workspace.element_size(),
          flags, _stream(stream))
     return out
+
+
+def w4a6_linear(x: torch.Tensor, weights: PackedWeights, bias: Optional[torch.Tensor] = None,
+                out_dtype=torch.bfloat16, epilogue: str = "none", out: Optional[torch.Tensor] = None,
+                workspace=None, stream=None) -> torch.Tensor:
+    """C = quantise_mxfp6(x) . W^T * tensor_scale (+ bias, activation) from raw activations x
+    (M, K) fp32/bf16 on the GPU: the on-device MXFP6 quantiser, then the W4A6 GEMM, both
+    launched with programmatic serialisation: the quantiser starts as the previous kernel on the
+    stream ends, and the GEMM's CTAs take the SMs the quantiser leaves free and stream the
+    (static) weights while it finishes; each reads its inputs only after its predecessor."""
+    acts = quantize_activations(x, stream, overlap_prev=True)
+    return w4a6_gemm(acts, weights, bias=bias, out_dtype=out_dtype, epilogue=epilogue, out=out,
+                     workspace=workspace, stream=stream, overlap_prev=True, weights_static=True)
 
 
 def w4a6_gemm_noalloc(acts: PackedActivations, weights: PackedWeights, out: torch.Tensor,

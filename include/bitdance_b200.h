@@ -136,6 +136,15 @@ int bd_pack_a(const uint8_t* codes, const uint8_t* e8m0, uint8_t* a_packed,
 int bd_quantize_a_mxfp6(const void* x, int x_dtype, uint8_t* codes, uint8_t* e8m0,
                         uint8_t* scales_tiled, int M, int K, bd_stream_t stream);
 
+/* bd_quantize_a_mxfp6 with launch flags: BD_GEMM_OVERLAP_PREV launches it with programmatic
+ * stream serialisation (it may be scheduled while the previous kernel on the stream ends, and
+ * waits for it before reading x or writing its outputs). Either way the kernel lets a GEMM
+ * launched after it with BD_GEMM_OVERLAP_PREV start early (that GEMM reads the codes only
+ * after this kernel completes). No reference counterpart. */
+int bd_quantize_a_mxfp6_ex(const void* x, int x_dtype, uint8_t* codes, uint8_t* e8m0,
+                           uint8_t* scales_tiled, int M, int K, unsigned flags,
+                           bd_stream_t stream);
+
 /* Weights w (N, K) row-major, fp32 or bf16 -> NVFP4 with per-16 E4M3 scales and an fp32
  * per-tensor scale, the natural layouts bd_pack_b takes: codes (N, K/2) E2M1 nibbles (element
  * 2j in the low nibble of byte j), scales16 (N, K/16) E4M3 bytes. tstat is a device buffer of

@@ -120,6 +120,9 @@ def test_quantize_rejects_bad_arguments():
     assert q(ok, 1, ok, ok, None, 0, 128, None) == -2        # M <= 0
     assert q(P(4104), 0, ok, ok, None, 4, 128, None) == -3   # x not 16-byte aligned
     assert q(ok, 0, P(4097), ok, None, 4, 128, None) == -3   # codes not 16-byte aligned
+    qx = lib.bd_quantize_a_mxfp6_ex
+    assert qx(ok, 0, ok, ok, None, 4, 128, 2, None) == -1     # unknown launch flag
+    assert qx(ok, 0, ok, ok, None, 4, 48, 1, None) == -2      # then the same checks
 
 
 # ---------------------------------------------------------------------------------------
@@ -209,4 +212,27 @@ def test_gpu_non_finite_input_sets_the_error_bit():
         bd.quantize_mxfp6(x)
         assert bd.device_error() == _lib.BD_DEVERR_NONFINITE
     bd.quantize_mxfp6(torch.randn((4, 128), device="cuda"))
+    assert bd.device_error() == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M", [1, 16, 200])
+def test_gpu_linear_from_raw_activations(M):
+    """w4a6_linear (quantiser + programmatically launched GEMM) equals the GEMM of the separately
+    quantised activations bit for bit, and the oracle GEMM of the oracle's quantisation."""
+    import torch
+    import bitdance_b200 as bd
+    N, K = 512, 1024
+    rng = np.random.default_rng(M)
+    x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(torch.bfloat16).cuda()
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    wts = bd.quantize_weights(torch.from_numpy(w).cuda())
+    got = bd.w4a6_linear(x, wts)
+    ref = bd.w4a6_gemm(bd.quantize_activations(x), wts)
+    assert torch.equal(got, ref)
+    a_codes, a_e8 = o.quantize_a_mxfp6(x.float().cpu().numpy())
+    b_codes, b_sc, s_t = o.quantize_b_nvfp4(w, block=16)
+    e6, e8 = o.transcode_b(o.pack_nibbles(b_codes), b_sc, 16)
+    gold = o.gemm_gold(a_codes, a_e8, e6, e8, float(s_t))
+    assert o.rel_linf(gold, got.float().cpu().numpy()) <= 1e-2
     assert bd.device_error() == 0
