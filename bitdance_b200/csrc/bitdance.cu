@@ -580,7 +580,16 @@ int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const ui
 int bd_w4a6_gemm_noalloc(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8_t* b,
                          const uint8_t* b_scales, float b_tensor_scale, const void* bias, int M,
                          int N, int K, int out_dtype, int epilogue, bd_stream_t stream) {
+  // the argument checks of bd_w4a6_gemm, before any device call (the scratch clear below)
+  if (!c || !a || !a_scales || !b || !b_scales) return BD_ERR_INVALID_ARG;
+  if (out_dtype < BD_OUT_BF16 || out_dtype > BD_OUT_F32) return BD_ERR_INVALID_ARG;
+  if (epilogue < BD_EPI_NONE || epilogue > BD_EPI_BIAS_GELU) return BD_ERR_INVALID_ARG;
+  if (epilogue != BD_EPI_NONE && !bias) return BD_ERR_INVALID_ARG;
   if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % 128) return BD_ERR_SHAPE;
+  if (M > (1 << 30) / 4 || K > (1 << 24) || N > (1 << 24)) return BD_ERR_SHAPE;
+  if (!aligned(a, 16) || !aligned(a_scales, 16) || !aligned(b, 16) || !aligned(b_scales, 16) ||
+      (bias && !aligned(bias, 2)))
+    return BD_ERR_ALIGNMENT;
   DeviceInfo* d = nullptr;
   int st = device_info(&d);
   if (st != BD_OK) return st;
