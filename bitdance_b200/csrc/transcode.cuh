@@ -166,26 +166,46 @@ __global__ void __launch_bounds__(256) transcode_kernel(const uint4* __restrict_
   __shared__ TranscodeTables tab;
   load_tables<false>(tab, threadIdx.x, blockDim.x);
   __syncthreads();
+  // kUnroll independent blocks per thread per step (stride apart, so every load instruction is
+  // coalesced across the warp), all loaded before any is converted: enough bytes in flight per
+  // SM for the HBM latency
+  constexpr int kUnroll = 4;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; b < nblk;
-       b += stride) {
-    const uint4 q = ld_stream_u4(codes + b);
-    uint32_t s0, s1;
-    if constexpr (kScaleBlock == 16) {
-      const uint32_t s = reinterpret_cast<const uint16_t*>(scales)[b];
-      s0 = s & 0xFFu;
-      s1 = s >> 8;
-    } else {
-      s0 = s1 = scales[b];
+  for (int64_t b0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; b0 < nblk;
+       b0 += stride * kUnroll) {
+    uint4 q[kUnroll];
+    uint32_t sc[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t b = b0 + u * stride;
+      if (b < nblk) {
+        q[u] = ld_stream_u4(codes + b);
+        if constexpr (kScaleBlock == 16)
+          sc[u] = reinterpret_cast<const uint16_t*>(scales)[b];
+        else
+          sc[u] = scales[b];
+      }
     }
-    uint2 T0, T1;
-    uint32_t e8;
-    scale_pair(tab, s0, s1, T0, T1, e8);
-    uint4 o0, o1;
-    transcode32<false>(q, T0, T1, o0, o1);
-    st_stream_u4(e2m3 + 2 * b, o0);
-    st_stream_u4(e2m3 + 2 * b + 1, o1);
-    e8m0[b] = static_cast<uint8_t>(e8);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t b = b0 + u * stride;
+      if (b >= nblk) break;
+      uint32_t s0, s1;
+      if constexpr (kScaleBlock == 16) {
+        s0 = sc[u] & 0xFFu;
+        s1 = sc[u] >> 8;
+      } else {
+        s0 = s1 = sc[u];
+      }
+      uint2 T0, T1;
+      uint32_t e8;
+      scale_pair(tab, s0, s1, T0, T1, e8);
+      uint4 o0, o1;
+      transcode32<false>(q[u], T0, T1, o0, o1);
+      st_stream_u4(e2m3 + 2 * b, o0);
+      st_stream_u4(e2m3 + 2 * b + 1, o1);
+      e8m0[b] = static_cast<uint8_t>(e8);
+    }
   }
 }
 
