@@ -288,15 +288,15 @@ int bd_transcode_nvfp4_to_mxfp6(const uint8_t* codes, const uint8_t* scales, uin
   DeviceInfo* d = nullptr;
   int st = device_info(&d);
   if (st != BD_OK) return st;
-  const int grid = grid_for(nblk32, 256, d);
+  const int64_t stages = (nblk32 + kTxBlocks - 1) / kTxBlocks;
+  const int grid = static_cast<int>(std::min<int64_t>(stages, static_cast<int64_t>(d->sm_count) * 4));
+  const uint8_t* cb = reinterpret_cast<const uint8_t*>(codes);
   if (scale_block == 16)
-    transcode_kernel<16><<<grid, 256, 0, as_stream(stream)>>>(
-        reinterpret_cast<const uint4*>(codes), scales, reinterpret_cast<uint4*>(e2m3_out),
-        e8m0_out, nblk32);
+    transcode_kernel<16><<<grid, kTxThreads, 0, as_stream(stream)>>>(
+        cb, scales, reinterpret_cast<uint4*>(e2m3_out), e8m0_out, nblk32, d->err);
   else
-    transcode_kernel<32><<<grid, 256, 0, as_stream(stream)>>>(
-        reinterpret_cast<const uint4*>(codes), scales, reinterpret_cast<uint4*>(e2m3_out),
-        e8m0_out, nblk32);
+    transcode_kernel<32><<<grid, kTxThreads, 0, as_stream(stream)>>>(
+        cb, scales, reinterpret_cast<uint4*>(e2m3_out), e8m0_out, nblk32, d->err);
   return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
 }
 

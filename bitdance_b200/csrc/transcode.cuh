@@ -156,55 +156,94 @@ __device__ __forceinline__ void st_stream_u4(uint4* p, const uint4& v) {
 }
 
 // ---------------------------------------------------------------------------------------
-// Standalone transcode: natural layouts, one thread per 32-block, grid-stride.
+// Standalone transcode: natural layouts, one consumer lane per 32-block. A CTA is 8 consumer
+// warps and a producer warp whose lane 0 streams stages of 256 blocks' packed codes (4 KB,
+// contiguous) into a shared-memory ring with bulk copies; lane t converts block t of each
+// stage (its 16 bytes are read conflict-free) and loads the block's scale bytes from global
+// memory itself, before it waits for the stage. A stage is released after the codes converted
+// from it are stored (the stores depend on every word read from it).
+constexpr int kTxConsumerWarps = 8;
+constexpr int kTxThreads = 32 * (kTxConsumerWarps + 1);
+constexpr int kTxBlocks = 32 * kTxConsumerWarps;  // blocks per stage
+constexpr int kTxStageBytes = kTxBlocks * 16;
+constexpr int kTxStages = 6;
+
 template <int kScaleBlock>
-__global__ void __launch_bounds__(256) transcode_kernel(const uint4* __restrict__ codes,
-                                                        const uint8_t* __restrict__ scales,
-                                                        uint4* __restrict__ e2m3,
-                                                        uint8_t* __restrict__ e8m0,
-                                                        int64_t nblk) {
+__global__ void __launch_bounds__(kTxThreads, 4) transcode_kernel(const uint8_t* __restrict__ codes,
+                                                                 const uint8_t* __restrict__ scales,
+                                                                 uint4* __restrict__ e2m3,
+                                                                 uint8_t* __restrict__ e8m0,
+                                                                 int64_t nblk, uint32_t* err) {
   __shared__ TranscodeTables tab;
+  __shared__ __align__(128) uint8_t stage[kTxStages][kTxStageBytes];
+  __shared__ __align__(8) uint64_t full[kTxStages], empty[kTxStages];
+  __shared__ uint32_t abort_word;
+  volatile uint32_t* abort_flag = &abort_word;
   load_tables<false>(tab, threadIdx.x, blockDim.x);
-  __syncthreads();
-  // kUnroll independent blocks per thread per step (stride apart, so every load instruction is
-  // coalesced across the warp), all loaded before any is converted: enough bytes in flight per
-  // SM for the HBM latency
-  constexpr int kUnroll = 4;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t b0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; b0 < nblk;
-       b0 += stride * kUnroll) {
-    uint4 q[kUnroll];
-    uint32_t sc[kUnroll];
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int64_t b = b0 + u * stride;
-      if (b < nblk) {
-        q[u] = ld_stream_u4(codes + b);
-        if constexpr (kScaleBlock == 16)
-          sc[u] = reinterpret_cast<const uint16_t*>(scales)[b];
-        else
-          sc[u] = scales[b];
-      }
+  if (threadIdx.x == 0) {
+    abort_word = 0;
+    for (int i = 0; i < kTxStages; ++i) {
+      mbar_init(smem_u32(&full[i]), 1);
+      mbar_init(smem_u32(&empty[i]), kTxConsumerWarps);
     }
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int64_t b = b0 + u * stride;
-      if (b >= nblk) break;
-      uint32_t s0, s1;
-      if constexpr (kScaleBlock == 16) {
-        s0 = sc[u] & 0xFFu;
-        s1 = sc[u] >> 8;
-      } else {
-        s0 = s1 = sc[u];
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int64_t nstage = (nblk + kTxBlocks - 1) / kTxBlocks;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == kTxConsumerWarps) {
+    if (lane == 0) {
+      int64_t i = 0;
+      for (int64_t s = blockIdx.x; s < nstage; s += gridDim.x, ++i) {
+        const int slot = static_cast<int>(i % kTxStages);
+        const uint32_t ph = static_cast<uint32_t>(i / kTxStages) & 1u;
+        if (!mbar_wait(smem_u32(&empty[slot]), ph ^ 1u, err, kErrWaitEmpty, abort_flag)) break;
+        const int64_t left = nblk - s * kTxBlocks;
+        const uint32_t bytes = static_cast<uint32_t>(left < kTxBlocks ? left : kTxBlocks) * 16u;
+        mbar_arrive_expect_tx(smem_u32(&full[slot]), bytes);
+        bulk_load(smem_u32(stage[slot]), codes + s * kTxStageBytes, bytes, smem_u32(&full[slot]));
       }
-      uint2 T0, T1;
-      uint32_t e8;
-      scale_pair(tab, s0, s1, T0, T1, e8);
-      uint4 o0, o1;
-      transcode32<false>(q[u], T0, T1, o0, o1);
-      st_stream_u4(e2m3 + 2 * b, o0);
-      st_stream_u4(e2m3 + 2 * b + 1, o1);
-      e8m0[b] = static_cast<uint8_t>(e8);
+      // every copy issued has landed before the CTA exits: the last phase of each slot used
+      for (int64_t j = (i > kTxStages ? i - kTxStages : 0); j < i; ++j)
+        mbar_wait(smem_u32(&full[j % kTxStages]), static_cast<uint32_t>(j / kTxStages) & 1u,
+                  err, kErrWaitTma, nullptr);
+    }
+  } else {
+    const int t = threadIdx.x;
+    int64_t i = 0;
+    for (int64_t s = blockIdx.x; s < nstage; s += gridDim.x, ++i) {
+      const int slot = static_cast<int>(i % kTxStages);
+      const uint32_t ph = static_cast<uint32_t>(i / kTxStages) & 1u;
+      const int64_t b = s * kTxBlocks + t;
+      const bool valid = b < nblk;
+      uint32_t sc = 0;
+      if (valid) {
+        if constexpr (kScaleBlock == 16)
+          sc = reinterpret_cast<const uint16_t*>(scales)[b];
+        else
+          sc = scales[b];
+      }
+      if (!mbar_wait(smem_u32(&full[slot]), ph, err, kErrWaitTma, abort_flag)) break;
+      if (valid) {
+        const uint4 q = reinterpret_cast<const uint4*>(stage[slot])[t];
+        uint32_t s0, s1;
+        if constexpr (kScaleBlock == 16) {
+          s0 = sc & 0xFFu;
+          s1 = sc >> 8;
+        } else {
+          s0 = s1 = sc;
+        }
+        uint2 T0, T1;
+        uint32_t e8;
+        scale_pair(tab, s0, s1, T0, T1, e8);
+        uint4 o0, o1;
+        transcode32<false>(q, T0, T1, o0, o1);
+        st_stream_u4(e2m3 + 2 * b, o0);
+        st_stream_u4(e2m3 + 2 * b + 1, o1);
+        e8m0[b] = static_cast<uint8_t>(e8);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&empty[slot]));
     }
   }
 }
