@@ -90,7 +90,7 @@ struct GemmCfg {
   static constexpr int oSf = oB + SB * kBStage;  // SB x 256 E8M0 words staged for tensor memory
   // magnitude table, 8 copies interleaved (entry e of copy j at e*64 + j*8): lane l reads
   // copy l % 8
-  static constexpr int kPermCopies = 8;
+  static constexpr int kPermCopies = 8;  // a table row is 64 bytes: class words index it
   static constexpr int oPerm = oSf + SB * 1024;
   static constexpr int oTs = oPerm + 64 * 8 * kPermCopies;  // token scale ring
   static constexpr int oCtl = oTs + ST * kTScaleSlot;
@@ -128,7 +128,6 @@ struct GemmCtl {
   uint32_t fin_job;  // 1: this CTA finishes the tile of its last segment
   uint32_t abort_flag;
   uint32_t bcast;
-  TranscodeTables tab;
 };
 
 struct GemmParams {
@@ -200,37 +199,6 @@ struct Schedule {
   }
 };
 
-// Magnitude-table rows (d*8 + mb) of the two 16-blocks of a 32-block and its E8M0 byte, from
-// the two E4M3 scale bytes. A normal scale byte s has mantissa bits s & 7 and bumped exponent
-// e = ((s & 0x7F) + 7) / 8 - 7 (exponent field + (mantissa != 0) - 7), so only subnormal and
-// zero scales read the class table.
-__device__ __forceinline__ void pair_class(const TranscodeTables& t, uint32_t s0, uint32_t s1,
-                                           uint32_t& i0, uint32_t& i1, uint32_t& e8) {
-  const uint32_t x0 = s0 & 0x7Fu, x1 = s1 & 0x7Fu;
-  int ep0, ep1;  // e + 7
-  uint32_t mb0, mb1;
-  if (x0 & 0x78u) {
-    ep0 = static_cast<int>((x0 + 7u) >> 3);
-    mb0 = x0 & 7u;
-  } else {
-    const uint32_t v = t.info[x0];
-    ep0 = static_cast<int>(v >> 3) - 9;
-    mb0 = v & 7u;
-  }
-  if (x1 & 0x78u) {
-    ep1 = static_cast<int>((x1 + 7u) >> 3);
-    mb1 = x1 & 7u;
-  } else {
-    const uint32_t v = t.info[x1];
-    ep1 = static_cast<int>(v >> 3) - 9;
-    mb1 = v & 7u;
-  }
-  const int em = max(ep0, ep1);
-  i0 = static_cast<uint32_t>(min(em - ep0, 7)) * 8u + mb0;
-  i1 = static_cast<uint32_t>(min(em - ep1, 7)) * 8u + mb1;
-  e8 = static_cast<uint32_t>(em + 120);  // e + 127
-}
-
 __device__ __forceinline__ float apply_epilogue(float v, int epi, const __nv_bfloat16* bias,
                                                 int n) {
   if (epi != 0) v += __bfloat162float(bias[n]);
@@ -293,21 +261,14 @@ __device__ __forceinline__ void store_row(void* out, int64_t idx, const float (&
   }
 }
 
-// Eight E2M1 nibbles (one word) -> eight E4M3 bytes (two words) with the magnitude table
-// T of the 16-block's class. Signs: byte i of (w<<4) / w carries the sign of element 2i /
-// 2i+1 in bit 7, so one prmt gathers four of them.
+// Eight E2M1 codes of a transcode-ready word (magnitudes in nibble bits 0..2; the signs of
+// elements 0..3 at bits 7, 15, 23, 31 and of elements 4..7 at bits 3, 11, 19, 27) -> eight E4M3
+// bytes, with the magnitude table T of the 16-block's class: one prmt per four magnitudes, the
+// signs merged in place.
 __device__ __forceinline__ void nib8_to_e4m3(uint32_t w, uint2 T, uint32_t& lo, uint32_t& hi) {
   const uint32_t m = w & 0x77777777u;
-  const uint32_t t = w << 4;
-  lo = (prmt(t, w, 0x5140u) & 0x80808080u) | prmt(T.x, T.y, m);
-  hi = (prmt(t, w, 0x7362u) & 0x80808080u) | prmt(T.x, T.y, m >> 16);
-}
-
-// E8M0 byte of a 32-block from its two E4M3 scale bytes.
-__device__ __forceinline__ uint32_t e8m0_of_pair(const TranscodeTables& t, uint32_t s0,
-                                                 uint32_t s1) {
-  const int e0 = t.info[s0 & 0x7Fu] >> 3, e1 = t.info[s1 & 0x7Fu] >> 3;
-  return static_cast<uint32_t>(max(e0, e1) + 111);
+  lo = prmt(T.x, T.y, m) | (w & 0x80808080u);
+  hi = prmt(T.x, T.y, m >> 16) | ((w << 4) & 0x80808080u);
 }
 
 // Stream-K fix-up of one tile: C = sum of the contributors' fp32 partial slots, added in CTA
@@ -442,7 +403,6 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
       tmem_relinquish();
     } else if (warp >= 2 + Cfg::kEpiWarps) {
       const int t0 = tid - 32 * (2 + Cfg::kEpiWarps);
-      load_tables<true>(ctl.tab, t0, 32 * Cfg::kTranscodeWarps);
       const uint2* src = reinterpret_cast<const uint2*>(&g_tables_e4m3);  // perm[] comes first
       uint2* rep = reinterpret_cast<uint2*>(smem + Cfg::oPerm);
       for (int i = t0; i < 64 * Cfg::kPermCopies; i += 32 * Cfg::kTranscodeWarps)
@@ -608,14 +568,17 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         uint32_t* sf_stage = reinterpret_cast<uint32_t*>(smem + Cfg::oSf + bs * 1024);
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-          uint32_t sfw = 0;
 #pragma unroll
           for (int blk = 0; blk < 4; ++blk) {
-            const uint32_t pair = blk < 2 ? (sc[r].x >> (16 * blk)) : (sc[r].y >> (16 * (blk - 2)));
-            uint32_t i0, i1, e8;
-            pair_class(ctl.tab, pair & 0xFFu, (pair >> 8) & 0xFFu, i0, i1, e8);
-            const uint2 T0 = *reinterpret_cast<const uint2*>(perm + i0 * (8 * Cfg::kPermCopies));
-            const uint2 T1 = *reinterpret_cast<const uint2*>(perm + i1 * (8 * Cfg::kPermCopies));
+            // class word of the 32-block (written by the packer): the two 16-blocks' table rows
+            // times 64 (the byte stride of a row in the 8-copy table)
+            const uint32_t f = blk < 2 ? (sc[r].x >> (16 * blk)) : (sc[r].y >> (16 * (blk - 2)));
+            const uint32_t off_small = (f << 6) & 0xFC0u, off_big = f & 0x1C0u;
+            const bool first_big = (f & 0x200u) != 0;
+            const uint2 T0 =
+                *reinterpret_cast<const uint2*>(perm + (first_big ? off_big : off_small));
+            const uint2 T1 =
+                *reinterpret_cast<const uint2*>(perm + (first_big ? off_small : off_big));
             uint32_t v[8];
             nib8_to_e4m3(q[r][blk].x, T0, v[0], v[1]);
             nib8_to_e4m3(q[r][blk].y, T0, v[2], v[3]);
@@ -623,9 +586,11 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
             nib8_to_e4m3(q[r][blk].w, T1, v[6], v[7]);
             st_shared_v4(bt + b_row[r] + (((2 * blk) ^ r7[r]) << 4), v[0], v[1], v[2], v[3]);
             st_shared_v4(bt + b_row[r] + (((2 * blk + 1) ^ r7[r]) << 4), v[4], v[5], v[6], v[7]);
-            sfw |= e8 << (8 * blk);
           }
-          sf_stage[rows[r]] = sfw;
+          // E8M0 bytes of the row's four 32-blocks: class-word bits 10..14 + 118
+          sf_stage[rows[r]] =
+              prmt((sc[r].x >> 10) & 0x001F001Fu, (sc[r].y >> 10) & 0x001F001Fu, 0x6420u) +
+              0x76767676u;
         }
         fence_proxy_async_smem();  // the tensor core reads the B tile through the async proxy
         __syncwarp();

@@ -251,6 +251,33 @@ __global__ void __launch_bounds__(kTxThreads, 4) transcode_kernel(const uint8_t*
 // ---------------------------------------------------------------------------------------
 // Layout kernels.
 
+// The weights are static, so the tiled layout the GEMM reads carries the parts of the transcode
+// that depend on them alone, prepared once here:
+//  * code words: in each 32-bit word of E2M1 codes (elements 0..7 in nibbles 0..7) the
+//    magnitudes stay in nibble bits 0..2 and the sign of element i moves to bit 8i + 7 (i < 4)
+//    or 8(i - 4) + 3 (i >= 4), where an E4M3 byte of the low or (shifted by 4) high output word
+//    carries it;
+//  * per 32-block a 16-bit class word instead of the two E4M3 scale bytes (same size), from the
+//    scale-byte classes c = (e + 16) << 3 | mb (e = exponent + bump, 7..25; the info table):
+//    bits 0..5 the magnitude-table row d*8 + mb of the 16-block with the smaller e (d = the
+//    exponent gap, at most 7), bits 6..8 the mantissa bits of the other (its row, d = 0), bit 9
+//    set when that other one is the first 16-block, bits 10..14 emax - 7 (E8M0 = field + 118).
+__host__ __device__ constexpr uint32_t sign_spread(uint32_t w) {
+  uint32_t r = w & 0x77777777u;
+  for (int i = 0; i < 8; ++i)
+    r |= ((w >> (4 * i + 3)) & 1u) << (i < 4 ? 8 * i + 7 : 8 * (i - 4) + 3);
+  return r;
+}
+__host__ __device__ constexpr uint32_t pair_sideband(uint32_t c0, uint32_t c1) {
+  const uint32_t e0 = c0 >> 3, e1 = c1 >> 3;
+  const uint32_t first_big = e0 > e1 ? 1u : 0u;
+  const uint32_t em = first_big ? e0 : e1, es = first_big ? e1 : e0;
+  const uint32_t d = em - es < 7u ? em - es : 7u;
+  const uint32_t small_row = d * 8u + ((first_big ? c1 : c0) & 7u);
+  const uint32_t big_mb = (first_big ? c0 : c1) & 7u;
+  return small_row | (big_mb << 6) | (first_big << 9) | ((em - 7u) << 10);
+}
+
 // Natural B -> tiled: one thread per (row, 128-wide K chunk): 64 code bytes + 8 scale bytes.
 __global__ void pack_b_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ sc,
                               uint8_t* __restrict__ tcodes, uint8_t* __restrict__ tsc, int N,
@@ -266,10 +293,18 @@ __global__ void pack_b_kernel(const uint8_t* __restrict__ codes, const uint8_t* 
                                                       kc * 64);
     uint4* dst = reinterpret_cast<uint4*>(tcodes + tile * 8192 + r * 64);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) dst[j] = src[j];
-    const uint2 s = *reinterpret_cast<const uint2*>(sc + static_cast<int64_t>(row) * (K / 16) +
-                                                    kc * 8);
-    *reinterpret_cast<uint2*>(tsc + tile * 1024 + r * 8) = s;
+    for (int j = 0; j < 4; ++j) {
+      const uint4 v = src[j];
+      dst[j] = make_uint4(sign_spread(v.x), sign_spread(v.y), sign_spread(v.z), sign_spread(v.w));
+    }
+    const uint8_t* s = sc + static_cast<int64_t>(row) * (K / 16) + kc * 8;
+    uint32_t f[4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+      f[b] = pair_sideband(g_tables_e4m3.info[s[2 * b] & 0x7Fu],
+                           g_tables_e4m3.info[s[2 * b + 1] & 0x7Fu]);
+    *reinterpret_cast<uint2*>(tsc + tile * 1024 + r * 8) =
+        make_uint2(f[0] | (f[1] << 16), f[2] | (f[3] << 16));
   }
 }
 

@@ -68,9 +68,11 @@ def transcode(codes: torch.Tensor, scales: torch.Tensor, scale_block: int = 16,
 
 @dataclass
 class PackedWeights:
-    """NVFP4 weights in the GEMM's tiled layout (per-16 E4M3 scales + fp32 tensor scale)."""
+    """NVFP4 weights in the GEMM's tiled, transcode-ready layout (bd_pack_b): E2M1 codes with
+    their sign bits placed for the on-chip transcode, one 16-bit class word per 32-block made
+    from its two E4M3 scale bytes, and the fp32 tensor scale."""
     codes: torch.Tensor    # [N/128][K/128][128][64] u8 (flat)
-    scales: torch.Tensor   # [N/128][K/128][128][8]  u8 (flat)
+    scales: torch.Tensor   # [N/128][K/128][128][8]  u8 (flat): 4 class words per row and chunk
     tensor_scale: float
     N: int
     K: int

@@ -13,7 +13,8 @@ with the reference's argument order and meaning:
   buffer of partial planes the caller sums; with "atomic" an fp32 (M, N) buffer the caller
   zeroes.
 * arg_a: (M, K) u8 MXFP6 activations, arg_scale_a: E8M0 bytes, arg_b: (N, K/2) u8 NVFP4
-  codes, arg_scale_b: E4M3 bytes -- in this library's layouts (``ops.pack_activations`` /
+  codes, arg_scale_b: the per-16 scale sideband (one 16-bit class word per 32-block, made
+  from the two E4M3 bytes) -- in this library's layouts (``ops.pack_activations`` /
   ``ops.pack_weights``), which fit the reference's buffer sizes ``(M*K)//32*2+4096`` and
   ``(N*K)//32*2+4096`` bytes.
 * arg_bias: N bf16; arg_lut: accepted and ignored (the transcode tables are compiled into

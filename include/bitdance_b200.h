@@ -12,9 +12,15 @@
  *   NVFP4 weights B, "natural" layout:  codes (N, K/2) u8, element 2j in the low nibble of
  *       byte j (E2M1 nibble = sign<<3 | magnitude index); scales (N, K/16) E4M3 bytes (or
  *       (N, K/32) when scale_block == 32); one fp32 tensor scale.
- *   NVFP4 weights B, "tiled" layout used by the GEMM (bd_pack_b produces it):
- *       codes  [N/128][K/128][128 rows][64 bytes]   (same bytes, regrouped)
- *       scales [N/128][K/128][128 rows][8 bytes]
+ *   NVFP4 weights B, "tiled" layout used by the GEMM (bd_pack_b produces it; same byte
+ *   count as the natural layout, prepared for the on-chip transcode):
+ *       codes  [N/128][K/128][128 rows][64 bytes]: in each 32-bit word (elements 0..7 in
+ *              nibbles 0..7) the magnitudes stay in nibble bits 0..2 and the sign of element
+ *              i sits at bit 8i+7 (i < 4) or 8(i-4)+3 (i >= 4)
+ *       scales [N/128][K/128][128 rows][8 bytes]: per 32-block a 16-bit class word made from
+ *              its two E4M3 bytes -- bits 0..5 the magnitude-table row (d*8 + mb) of the
+ *              16-block with the smaller exponent, bits 6..8 the other's mantissa bits, bit 9
+ *              set when the other is the first 16-block, bits 10..14 E8M0 - 118
  *   MXFP6 activations A (bd_pack_a produces both from natural codes and scales):
  *       codes  (M, K) u8: one E2M3 code per byte (bits 0..5; bits 6..7 are ignored), the
  *              byte image the tensor core takes from tensor memory.

@@ -298,10 +298,12 @@ def test_repeated_calls_are_bitwise_identical(split_k):
     assert bd.device_error() == 0
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 14336, 4096), (1024, 4096, 4096)])
+@pytest.mark.parametrize("M,N,K", [(128, 14336, 4096), (1024, 4096, 4096), (16, 14336, 8192),
+                                   (32, 14336, 8192)])
 def test_streamk_long_segments_full_token_tile(M, N, K):
-    """128-row token tiles under stream-K with 12..27 K chunks per CTA: most CTAs run the tail
-    of one tile, store its partial, then start the next tile while the weight ring is full.
+    """Stream-K with 12..27 K chunks per CTA (128-row token tiles) and 24 per CTA (16- and
+    32-row decode tiles): most CTAs run the tail of one tile, store its partial, then start
+    the next tile while the rings are full.
     Every call is checked against the oracle (a weight stage released before its reads were
     performed showed up here as rows converted from a later chunk, on some calls only)."""
     import bitdance_b200 as bd
