@@ -37,15 +37,6 @@ __device__ __forceinline__ uint32_t nib4_to_e2m3(uint32_t x, uint32_t lo, uint32
   return mag | (sgn & 0x20202020u);
 }
 
-// Four E2M1 nibbles -> four E4M3 bytes carrying the same MXFP6 values (E2M3 values are
-// exactly representable in E4M3). A table of 0x01 bytes yields 0x01 (+) / 0x00 (-); moved
-// to bit 7 it flips the sign bit that the OR set.
-__device__ __forceinline__ uint32_t nib4_to_e4m3(uint32_t x, uint32_t lo, uint32_t hi) {
-  const uint32_t mag = prmt(lo, hi, x & 0x7777u);
-  const uint32_t pos = prmt(0x01010101u, 0x01010101u, x);
-  return (mag | 0x80808080u) ^ (pos << 7);
-}
-
 // Scale-byte class table: kScaleInfo[byte & 0x7F] = (e + 16) << 3 | mb, e = exponent + bump.
 struct ScaleInfoTable {
   uint8_t v[128];
@@ -125,21 +116,13 @@ __device__ __forceinline__ void scale_pair(const TranscodeTables& t, uint32_t s0
   e8m0 = static_cast<uint32_t>(emax + 111);  // (e + 16) - 16 + 127
 }
 
-// 32 nibbles (q) -> 32 output bytes (o0: elements 0..15, o1: 16..31).
-template <bool kE4M3>
+// 32 nibbles (q) -> 32 E2M3 code bytes (o0: elements 0..15, o1: 16..31).
 __device__ __forceinline__ void transcode32(const uint4& q, const uint2& T0, const uint2& T1,
                                             uint4& o0, uint4& o1) {
-  if constexpr (kE4M3) {
-    o0 = make_uint4(nib4_to_e4m3(q.x, T0.x, T0.y), nib4_to_e4m3(q.x >> 16, T0.x, T0.y),
-                    nib4_to_e4m3(q.y, T0.x, T0.y), nib4_to_e4m3(q.y >> 16, T0.x, T0.y));
-    o1 = make_uint4(nib4_to_e4m3(q.z, T1.x, T1.y), nib4_to_e4m3(q.z >> 16, T1.x, T1.y),
-                    nib4_to_e4m3(q.w, T1.x, T1.y), nib4_to_e4m3(q.w >> 16, T1.x, T1.y));
-  } else {
-    o0 = make_uint4(nib4_to_e2m3(q.x, T0.x, T0.y), nib4_to_e2m3(q.x >> 16, T0.x, T0.y),
-                    nib4_to_e2m3(q.y, T0.x, T0.y), nib4_to_e2m3(q.y >> 16, T0.x, T0.y));
-    o1 = make_uint4(nib4_to_e2m3(q.z, T1.x, T1.y), nib4_to_e2m3(q.z >> 16, T1.x, T1.y),
-                    nib4_to_e2m3(q.w, T1.x, T1.y), nib4_to_e2m3(q.w >> 16, T1.x, T1.y));
-  }
+  o0 = make_uint4(nib4_to_e2m3(q.x, T0.x, T0.y), nib4_to_e2m3(q.x >> 16, T0.x, T0.y),
+                  nib4_to_e2m3(q.y, T0.x, T0.y), nib4_to_e2m3(q.y >> 16, T0.x, T0.y));
+  o1 = make_uint4(nib4_to_e2m3(q.z, T1.x, T1.y), nib4_to_e2m3(q.z >> 16, T1.x, T1.y),
+                  nib4_to_e2m3(q.w, T1.x, T1.y), nib4_to_e2m3(q.w >> 16, T1.x, T1.y));
 }
 
 __device__ __forceinline__ uint4 ld_stream_u4(const uint4* p) {
@@ -237,7 +220,7 @@ __global__ void __launch_bounds__(kTxThreads, 4) transcode_kernel(const uint8_t*
         uint32_t e8;
         scale_pair(tab, s0, s1, T0, T1, e8);
         uint4 o0, o1;
-        transcode32<false>(q, T0, T1, o0, o1);
+        transcode32(q, T0, T1, o0, o1);
         st_stream_u4(e2m3 + 2 * b, o0);
         st_stream_u4(e2m3 + 2 * b + 1, o1);
         e8m0[b] = static_cast<uint8_t>(e8);
