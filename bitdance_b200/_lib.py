@@ -25,7 +25,7 @@ BD_ERR_DEVICE = -7
 BD_OUT_BF16, BD_OUT_F16, BD_OUT_F32 = 0, 1, 2
 BD_EPI_NONE, BD_EPI_BIAS, BD_EPI_BIAS_RELU, BD_EPI_BIAS_SILU, BD_EPI_BIAS_GELU = 0, 1, 2, 3, 4
 BD_SPLIT_REDUCE, BD_SPLIT_PLANES, BD_SPLIT_ATOMIC = 0, 1, 2
-BD_GEMM_OVERLAP_PREV, BD_GEMM_WEIGHTS_STATIC = 1, 2
+BD_GEMM_OVERLAP_PREV, BD_GEMM_WEIGHTS_STATIC, BD_GEMM_B_E4M3 = 1, 2, 4
 BD_IN_F32, BD_IN_BF16 = 0, 1
 BD_DEVERR_WAIT_MASK, BD_DEVERR_WAIT_TMA, BD_DEVERR_NONFINITE = 0x1F, 0x01, 0x20
 
@@ -42,6 +42,7 @@ SIGNATURES = {
     "bd_selftest_bounded_wait": (_I, [_I64, _P]),
     "bd_transcode_nvfp4_to_mxfp6": (_I, [_P, _P, _P, _P, _I64, _I, _P]),
     "bd_pack_b": (_I, [_P, _P, _P, _P, _I, _I, _P]),
+    "bd_pack_b_e4m3": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "bd_pack_a": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "bd_quantize_a_mxfp6": (_I, [_P, _I, _P, _P, _P, _I, _I, _P]),
     "bd_quantize_b_nvfp4": (_I, [_P, _I, _P, _P, _P, _I, _I, _P]),

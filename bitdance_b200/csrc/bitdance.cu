@@ -191,7 +191,7 @@ struct GemmMaps {
   CUtensorMap a, as, w, ws;
 };
 
-template <int BM>
+template <int BM, bool kClassWords>
 int launch_gemm(const GemmMaps& m, const GemmParams& p, int grid, bool overlap,
                 cudaStream_t stream) {
   using Cfg = GemmCfg<BM>;
@@ -200,7 +200,8 @@ int launch_gemm(const GemmMaps& m, const GemmParams& p, int grid, bool overlap,
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load() & bit)) {
-    if (cudaFuncSetAttribute(w4a6_gemm_kernel<BM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(w4a6_gemm_kernel<BM, kClassWords>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Cfg::kSmemBytes) != cudaSuccess)
       return BD_ERR_CUDA;
     configured.fetch_or(bit);
@@ -215,19 +216,27 @@ int launch_gemm(const GemmMaps& m, const GemmParams& p, int grid, bool overlap,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = overlap ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, w4a6_gemm_kernel<BM>, m.a, m.as, m.w, m.ws, p) != cudaSuccess)
+  if (cudaLaunchKernelEx(&cfg, w4a6_gemm_kernel<BM, kClassWords>, m.a, m.as, m.w, m.ws, p) !=
+      cudaSuccess)
     return BD_ERR_CUDA;
   return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
 }
 
-int launch_gemm_any(int bm, const GemmMaps& m, const GemmParams& p, int grid, bool overlap,
-                    cudaStream_t s) {
+template <bool kClassWords>
+int launch_gemm_bm(int bm, const GemmMaps& m, const GemmParams& p, int grid, bool overlap,
+                   cudaStream_t s) {
   switch (bm) {
-    case 16: return launch_gemm<16>(m, p, grid, overlap, s);
-    case 32: return launch_gemm<32>(m, p, grid, overlap, s);
-    case 64: return launch_gemm<64>(m, p, grid, overlap, s);
-    default: return launch_gemm<128>(m, p, grid, overlap, s);
+    case 16: return launch_gemm<16, kClassWords>(m, p, grid, overlap, s);
+    case 32: return launch_gemm<32, kClassWords>(m, p, grid, overlap, s);
+    case 64: return launch_gemm<64, kClassWords>(m, p, grid, overlap, s);
+    default: return launch_gemm<128, kClassWords>(m, p, grid, overlap, s);
   }
+}
+
+int launch_gemm_any(int bm, bool class_words, const GemmMaps& m, const GemmParams& p, int grid,
+                    bool overlap, cudaStream_t s) {
+  return class_words ? launch_gemm_bm<true>(bm, m, p, grid, overlap, s)
+                     : launch_gemm_bm<false>(bm, m, p, grid, overlap, s);
 }
 
 }  // namespace
@@ -300,8 +309,8 @@ int bd_transcode_nvfp4_to_mxfp6(const uint8_t* codes, const uint8_t* scales, uin
   return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
 }
 
-int bd_pack_b(const uint8_t* codes, const uint8_t* scales16, uint8_t* codes_tiled,
-              uint8_t* scales_tiled, int N, int K, bd_stream_t stream) {
+static int pack_b(const uint8_t* codes, const uint8_t* scales16, uint8_t* codes_tiled,
+                  uint8_t* scales_tiled, int N, int K, bool class_words, bd_stream_t stream) {
   if (!codes || !scales16 || !codes_tiled || !scales_tiled) return BD_ERR_INVALID_ARG;
   if (N <= 0 || K <= 0 || N % 128 || K % 128) return BD_ERR_SHAPE;
   if (!aligned(codes, 16) || !aligned(codes_tiled, 16) || !aligned(scales16, 8) ||
@@ -311,10 +320,23 @@ int bd_pack_b(const uint8_t* codes, const uint8_t* scales16, uint8_t* codes_tile
   int st = device_info(&d);
   if (st != BD_OK) return st;
   const int64_t work = static_cast<int64_t>(N) * (K / 128);
-  pack_b_kernel<<<grid_for(work, 256, d), 256, 0, as_stream(stream)>>>(codes, scales16,
-                                                                        codes_tiled, scales_tiled,
-                                                                        N, K);
+  if (class_words)
+    pack_b_kernel<true><<<grid_for(work, 256, d), 256, 0, as_stream(stream)>>>(
+        codes, scales16, codes_tiled, scales_tiled, N, K);
+  else
+    pack_b_kernel<false><<<grid_for(work, 256, d), 256, 0, as_stream(stream)>>>(
+        codes, scales16, codes_tiled, scales_tiled, N, K);
   return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
+}
+
+int bd_pack_b(const uint8_t* codes, const uint8_t* scales16, uint8_t* codes_tiled,
+              uint8_t* scales_tiled, int N, int K, bd_stream_t stream) {
+  return pack_b(codes, scales16, codes_tiled, scales_tiled, N, K, true, stream);
+}
+
+int bd_pack_b_e4m3(const uint8_t* codes, const uint8_t* scales16, uint8_t* codes_tiled,
+                   uint8_t* scales_tiled, int N, int K, bd_stream_t stream) {
+  return pack_b(codes, scales16, codes_tiled, scales_tiled, N, K, false, stream);
 }
 
 int bd_pack_a(const uint8_t* codes, const uint8_t* e8m0, uint8_t* a_packed, uint8_t* scales_tiled,
@@ -482,7 +504,8 @@ int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const ui
                     const uint8_t* b_scales, float b_tensor_scale, const void* bias, int M, int N,
                     int K, int split_k, int split_mode, int out_dtype, int epilogue,
                     void* workspace, size_t workspace_bytes, unsigned flags, bd_stream_t stream) {
-  if (flags & ~static_cast<unsigned>(BD_GEMM_OVERLAP_PREV | BD_GEMM_WEIGHTS_STATIC))
+  if (flags & ~static_cast<unsigned>(BD_GEMM_OVERLAP_PREV | BD_GEMM_WEIGHTS_STATIC |
+                                     BD_GEMM_B_E4M3))
     return BD_ERR_INVALID_ARG;
   if (!c || !a || !a_scales || !b || !b_scales) return BD_ERR_INVALID_ARG;
   if (out_dtype < BD_OUT_BF16 || out_dtype > BD_OUT_F32) return BD_ERR_INVALID_ARG;
@@ -570,7 +593,8 @@ int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const ui
     p.counters = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + sk.slots_bytes);
   }
   const int grid = static_cast<int>(work < d->sm_count ? work : d->sm_count);
-  const int rc = launch_gemm_any(bm, maps, p, grid, (flags & BD_GEMM_OVERLAP_PREV) != 0,
+  const int rc = launch_gemm_any(bm, (flags & BD_GEMM_B_E4M3) == 0, maps, p, grid,
+                                 (flags & BD_GEMM_OVERLAP_PREV) != 0,
                                  as_stream(stream));
   if (rc != BD_OK || !use_ws) return rc;
   return bd_splitk_reduce(static_cast<const float*>(workspace), c, bias, b_tensor_scale, M, N,

@@ -128,6 +128,7 @@ struct GemmCtl {
   uint32_t fin_job;  // 1: this CTA finishes the tile of its last segment
   uint32_t abort_flag;
   uint32_t bcast;
+  TranscodeTables tab;  // scale-byte classes (E4M3 sideband only)
 };
 
 struct GemmParams {
@@ -271,6 +272,30 @@ __device__ __forceinline__ void nib8_to_e4m3(uint32_t w, uint2 T, uint32_t& lo, 
   hi = prmt(T.x, T.y, m >> 16) | ((w << 4) & 0x80808080u);
 }
 
+// The same for a word of E2M1 codes as the reference stores them (sign in bit 3 of each
+// nibble): byte i of (w<<4) / w carries the sign of element 2i / 2i+1 in bit 7, so one prmt
+// gathers four of them.
+__device__ __forceinline__ void nib8_natural_to_e4m3(uint32_t w, uint2 T, uint32_t& lo,
+                                                     uint32_t& hi) {
+  const uint32_t m = w & 0x77777777u;
+  const uint32_t t = w << 4;
+  lo = (prmt(t, w, 0x5140u) & 0x80808080u) | prmt(T.x, T.y, m);
+  hi = (prmt(t, w, 0x7362u) & 0x80808080u) | prmt(T.x, T.y, m >> 16);
+}
+
+// Table rows (d*8 + mb) of the two 16-blocks of a 32-block and its E8M0 byte, from the two
+// E4M3 scale bytes (the E4M3 sideband): the classes (e + 16) << 3 | mb come from the table,
+// d = min(emax - e, 7), E8M0 = emax + 111.
+__device__ __forceinline__ void pair_class(const TranscodeTables& t, uint32_t s0, uint32_t s1,
+                                           uint32_t& i0, uint32_t& i1, uint32_t& e8) {
+  const uint32_t c0 = t.info[s0 & 0x7Fu], c1 = t.info[s1 & 0x7Fu];
+  const int e0 = static_cast<int>(c0 >> 3), e1 = static_cast<int>(c1 >> 3);
+  const int em = max(e0, e1);
+  i0 = static_cast<uint32_t>(min(em - e0, 7)) * 8u + (c0 & 7u);
+  i1 = static_cast<uint32_t>(min(em - e1, 7)) * 8u + (c1 & 7u);
+  e8 = static_cast<uint32_t>(em + 111);
+}
+
 // Stream-K fix-up of one tile: C = sum of the contributors' fp32 partial slots, added in CTA
 // order (first..last), times the tensor scale, bias and activation. Worker `worker` of
 // `nworkers` takes float4 groups worker, worker + nworkers, ...; loads of up to four
@@ -349,7 +374,9 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                : "memory");
 }
 
-template <int BM>
+// kClassWords: B in bd_pack_b's transcode-ready layout (moved sign bits, class words); else
+// the E4M3 sideband (bd_pack_b_e4m3: the reference's codes and scale bytes, regrouped).
+template <int BM, bool kClassWords>
 __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
     w4a6_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
                      const __grid_constant__ CUtensorMap tm_as,
@@ -403,6 +430,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
       tmem_relinquish();
     } else if (warp >= 2 + Cfg::kEpiWarps) {
       const int t0 = tid - 32 * (2 + Cfg::kEpiWarps);
+      if constexpr (!kClassWords) load_tables<true>(ctl.tab, t0, 32 * Cfg::kTranscodeWarps);
       const uint2* src = reinterpret_cast<const uint2*>(&g_tables_e4m3);  // perm[] comes first
       uint2* rep = reinterpret_cast<uint2*>(smem + Cfg::oPerm);
       for (int i = t0; i < 64 * Cfg::kPermCopies; i += 32 * Cfg::kTranscodeWarps)
@@ -568,29 +596,46 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         uint32_t* sf_stage = reinterpret_cast<uint32_t*>(smem + Cfg::oSf + bs * 1024);
 #pragma unroll
         for (int r = 0; r < R; ++r) {
+          uint32_t sfw = 0;
 #pragma unroll
           for (int blk = 0; blk < 4; ++blk) {
-            // class word of the 32-block (written by the packer): the two 16-blocks' table rows
-            // times 64 (the byte stride of a row in the 8-copy table)
             const uint32_t f = blk < 2 ? (sc[r].x >> (16 * blk)) : (sc[r].y >> (16 * (blk - 2)));
-            const uint32_t off_small = (f << 6) & 0xFC0u, off_big = f & 0x1C0u;
-            const bool first_big = (f & 0x200u) != 0;
-            const uint2 T0 =
-                *reinterpret_cast<const uint2*>(perm + (first_big ? off_big : off_small));
-            const uint2 T1 =
-                *reinterpret_cast<const uint2*>(perm + (first_big ? off_small : off_big));
+            uint32_t off0, off1;  // byte offsets of the two 16-blocks' table rows
+            if constexpr (kClassWords) {
+              // class word: both rows times 64 (the byte stride of a row in the 8-copy table)
+              const uint32_t off_small = (f << 6) & 0xFC0u, off_big = f & 0x1C0u;
+              const bool first_big = (f & 0x200u) != 0;
+              off0 = first_big ? off_big : off_small;
+              off1 = first_big ? off_small : off_big;
+            } else {
+              uint32_t i0, i1, e8;
+              pair_class(ctl.tab, f & 0xFFu, (f >> 8) & 0xFFu, i0, i1, e8);
+              off0 = i0 * (8 * Cfg::kPermCopies);
+              off1 = i1 * (8 * Cfg::kPermCopies);
+              sfw |= e8 << (8 * blk);
+            }
+            const uint2 T0 = *reinterpret_cast<const uint2*>(perm + off0);
+            const uint2 T1 = *reinterpret_cast<const uint2*>(perm + off1);
             uint32_t v[8];
-            nib8_to_e4m3(q[r][blk].x, T0, v[0], v[1]);
-            nib8_to_e4m3(q[r][blk].y, T0, v[2], v[3]);
-            nib8_to_e4m3(q[r][blk].z, T1, v[4], v[5]);
-            nib8_to_e4m3(q[r][blk].w, T1, v[6], v[7]);
+            if constexpr (kClassWords) {
+              nib8_to_e4m3(q[r][blk].x, T0, v[0], v[1]);
+              nib8_to_e4m3(q[r][blk].y, T0, v[2], v[3]);
+              nib8_to_e4m3(q[r][blk].z, T1, v[4], v[5]);
+              nib8_to_e4m3(q[r][blk].w, T1, v[6], v[7]);
+            } else {
+              nib8_natural_to_e4m3(q[r][blk].x, T0, v[0], v[1]);
+              nib8_natural_to_e4m3(q[r][blk].y, T0, v[2], v[3]);
+              nib8_natural_to_e4m3(q[r][blk].z, T1, v[4], v[5]);
+              nib8_natural_to_e4m3(q[r][blk].w, T1, v[6], v[7]);
+            }
             st_shared_v4(bt + b_row[r] + (((2 * blk) ^ r7[r]) << 4), v[0], v[1], v[2], v[3]);
             st_shared_v4(bt + b_row[r] + (((2 * blk + 1) ^ r7[r]) << 4), v[4], v[5], v[6], v[7]);
           }
-          // E8M0 bytes of the row's four 32-blocks: class-word bits 10..14 + 118
-          sf_stage[rows[r]] =
-              prmt((sc[r].x >> 10) & 0x001F001Fu, (sc[r].y >> 10) & 0x001F001Fu, 0x6420u) +
-              0x76767676u;
+          // E8M0 bytes of the row's four 32-blocks (class words: bits 10..14 + 118)
+          if constexpr (kClassWords)
+            sfw = prmt((sc[r].x >> 10) & 0x001F001Fu, (sc[r].y >> 10) & 0x001F001Fu, 0x6420u) +
+                  0x76767676u;
+          sf_stage[rows[r]] = sfw;
         }
         fence_proxy_async_smem();  // the tensor core reads the B tile through the async proxy
         __syncwarp();

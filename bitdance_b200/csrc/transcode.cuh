@@ -261,7 +261,9 @@ __host__ __device__ constexpr uint32_t pair_sideband(uint32_t c0, uint32_t c1) {
   return small_row | (big_mb << 6) | (first_big << 9) | ((em - 7u) << 10);
 }
 
-// Natural B -> tiled: one thread per (row, 128-wide K chunk): 64 code bytes + 8 scale bytes.
+// Natural B -> tiled: one thread per (row, 128-wide K chunk): 64 code bytes + 8 scale bytes,
+// transcode-ready (kClassWords) or only regrouped (the E4M3 sideband).
+template <bool kClassWords>
 __global__ void pack_b_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ sc,
                               uint8_t* __restrict__ tcodes, uint8_t* __restrict__ tsc, int N,
                               int K) {
@@ -275,19 +277,25 @@ __global__ void pack_b_kernel(const uint8_t* __restrict__ codes, const uint8_t* 
     const uint4* src = reinterpret_cast<const uint4*>(codes + static_cast<int64_t>(row) * (K / 2) +
                                                       kc * 64);
     uint4* dst = reinterpret_cast<uint4*>(tcodes + tile * 8192 + r * 64);
+    uint2* sdst = reinterpret_cast<uint2*>(tsc + tile * 1024 + r * 8);
+    const uint8_t* s = sc + static_cast<int64_t>(row) * (K / 16) + kc * 8;
+    if constexpr (!kClassWords) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dst[j] = src[j];
+      *sdst = *reinterpret_cast<const uint2*>(s);
+      continue;
+    }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const uint4 v = src[j];
       dst[j] = make_uint4(sign_spread(v.x), sign_spread(v.y), sign_spread(v.z), sign_spread(v.w));
     }
-    const uint8_t* s = sc + static_cast<int64_t>(row) * (K / 16) + kc * 8;
     uint32_t f[4];
 #pragma unroll
     for (int b = 0; b < 4; ++b)
       f[b] = pair_sideband(g_tables_e4m3.info[s[2 * b] & 0x7Fu],
                            g_tables_e4m3.info[s[2 * b + 1] & 0x7Fu]);
-    *reinterpret_cast<uint2*>(tsc + tile * 1024 + r * 8) =
-        make_uint2(f[0] | (f[1] << 16), f[2] | (f[3] << 16));
+    *sdst = make_uint2(f[0] | (f[1] << 16), f[2] | (f[3] << 16));
   }
 }
 

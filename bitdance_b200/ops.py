@@ -76,6 +76,9 @@ class PackedWeights:
     tensor_scale: float
     N: int
     K: int
+    # "class": bd_pack_b's transcode-ready layout; "e4m3": the natural codes and E4M3 scale bytes
+    # only regrouped (bd_pack_b_e4m3), read with BD_GEMM_B_E4M3
+    sideband: str = "class"
 
 
 @dataclass
@@ -88,16 +91,20 @@ class PackedActivations:
 
 
 def pack_weights(codes: torch.Tensor, scales16: torch.Tensor, tensor_scale: float = 1.0,
-                 stream=None) -> PackedWeights:
-    """codes (N, K/2) packed nibbles, scales16 (N, K/16) E4M3 -> PackedWeights."""
+                 stream=None, sideband: str = "class") -> PackedWeights:
+    """codes (N, K/2) packed nibbles, scales16 (N, K/16) E4M3 -> PackedWeights. sideband
+    "class" (default): the transcode-ready layout; "e4m3": the reference's bytes regrouped."""
+    if sideband not in ("class", "e4m3"):
+        raise ValueError(f"unknown sideband {sideband!r}")
     N, Kh = codes.shape
     K = Kh * 2
     _need(codes, torch.uint8, "codes")
     _need(scales16, torch.uint8, "scales16", N * K // 16)
     tc = torch.empty(N * K // 2, dtype=torch.uint8, device=codes.device)
     ts = torch.empty(N * K // 16, dtype=torch.uint8, device=codes.device)
-    call("bd_pack_b", _p(codes), _p(scales16), _p(tc), _p(ts), N, K, _stream(stream))
-    return PackedWeights(tc, ts, float(tensor_scale), N, K)
+    call("bd_pack_b" if sideband == "class" else "bd_pack_b_e4m3", _p(codes), _p(scales16),
+         _p(tc), _p(ts), N, K, _stream(stream))
+    return PackedWeights(tc, ts, float(tensor_scale), N, K, sideband)
 
 
 def pack_activations(codes: torch.Tensor, e8m0: torch.Tensor, stream=None,
@@ -261,7 +268,8 @@ def w4a6_gemm(acts: PackedActivations, weights: PackedWeights,
     if epi != _lib.BD_EPI_NONE and bias is None:
         raise ValueError(f"epilogue {epilogue!r} needs a bias")
     flags = (_lib.BD_GEMM_OVERLAP_PREV if overlap_prev else 0) | \
-        (_lib.BD_GEMM_WEIGHTS_STATIC if weights_static else 0)
+        (_lib.BD_GEMM_WEIGHTS_STATIC if weights_static else 0) | \
+        (_lib.BD_GEMM_B_E4M3 if weights.sideband == "e4m3" else 0)
     call("bd_w4a6_gemm_ex", _p(out), _p(acts.codes), _p(acts.scales), _p(weights.codes),
          _p(weights.scales), float(weights.tensor_scale), _p(bias), M, N, K, split_k,
          SPLIT_MODES[split_mode], _OUT[out_dtype], epi, _p(workspace),
@@ -294,6 +302,8 @@ def w4a6_gemm_noalloc(acts: PackedActivations, weights: PackedWeights, out: torc
         raise ValueError(f"K mismatch: activations {K}, weights {weights.K}")
     if out.dtype not in _OUT:
         raise ValueError(f"unsupported output dtype {out.dtype}")
+    if weights.sideband != "class":
+        raise ValueError("bd_w4a6_gemm_noalloc takes weights packed by bd_pack_b (sideband 'class')")
     _need(out, out.dtype, "out", M * N)
     if bias is not None:
         _need(bias, torch.bfloat16, "bias", N)

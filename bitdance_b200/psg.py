@@ -13,10 +13,12 @@ with the reference's argument order and meaning:
   buffer of partial planes the caller sums; with "atomic" an fp32 (M, N) buffer the caller
   zeroes.
 * arg_a: (M, K) u8 MXFP6 activations, arg_scale_a: E8M0 bytes, arg_b: (N, K/2) u8 NVFP4
-  codes, arg_scale_b: the per-16 scale sideband (one 16-bit class word per 32-block, made
-  from the two E4M3 bytes) -- in this library's layouts (``ops.pack_activations`` /
-  ``ops.pack_weights``), which fit the reference's buffer sizes ``(M*K)//32*2+4096`` and
-  ``(N*K)//32*2+4096`` bytes.
+  codes, arg_scale_b: E4M3 bytes -- the reference's bytes in this library's tiles
+  (``ops.pack_activations`` / ``ops.pack_weights(..., sideband="e4m3")``), which fit the
+  reference's buffer sizes ``(M*K)//32*2+4096`` and ``(N*K)//32*2+4096`` bytes. Buffers the
+  reference scripts fill with constant or random bytes mean the same here.
+  (``ops.w4a6_gemm`` with ``ops.pack_weights``' default layout is the faster native path: the
+  packer does the weight-only part of the transcode once.)
 * arg_bias: N bf16; arg_lut: accepted and ignored (the transcode tables are compiled into
   the kernel); M, N: ints; stream: a torch stream, a raw handle or None.
 
@@ -85,11 +87,11 @@ class W4A6Launcher:
             out = _lib.BD_OUT_F32
         epi = _EPI[self.epilogue]
         bias = _addr(arg_bias) if epi != _lib.BD_EPI_NONE else None
-        call("bd_w4a6_gemm", ctypes.c_void_p(_addr(arg_c)), ctypes.c_void_p(_addr(arg_a)),
+        call("bd_w4a6_gemm_ex", ctypes.c_void_p(_addr(arg_c)), ctypes.c_void_p(_addr(arg_a)),
              ctypes.c_void_p(_addr(arg_scale_a)), ctypes.c_void_p(_addr(arg_b)),
              ctypes.c_void_p(_addr(arg_scale_b)), float(b_tensor_scale),
              None if bias is None else ctypes.c_void_p(bias), M, N, self.K, self.split_k, mode,
-             out, epi, None, 0, _stream(stream))
+             out, epi, None, 0, _lib.BD_GEMM_B_E4M3, _stream(stream))
 
 
 @functools.lru_cache(maxsize=1024)

@@ -21,6 +21,10 @@
  *              its two E4M3 bytes -- bits 0..5 the magnitude-table row (d*8 + mb) of the
  *              16-block with the smaller exponent, bits 6..8 the other's mantissa bits, bit 9
  *              set when the other is the first 16-block, bits 10..14 E8M0 - 118
+ *   NVFP4 weights B, "E4M3 sideband" tiled layout (bd_pack_b_e4m3 produces it; the GEMM reads
+ *   it with BD_GEMM_B_E4M3): the natural codes and E4M3 scale bytes, only regrouped into the
+ *   tiles above, so buffers filled with constant or random bytes mean what they mean in the
+ *   reference's layout (kernel/verify_w4a6.py, kernel/bench_sweep.py).
  *   MXFP6 activations A (bd_pack_a produces both from natural codes and scales):
  *       codes  (M, K) u8: one E2M3 code per byte (bits 0..5; bits 6..7 are ignored), the
  *              byte image the tensor core takes from tensor memory.
@@ -114,6 +118,11 @@ int bd_transcode_nvfp4_to_mxfp6(const uint8_t* codes, const uint8_t* scales, uin
 int bd_pack_b(const uint8_t* codes, const uint8_t* scales16, uint8_t* codes_tiled,
               uint8_t* scales_tiled, int N, int K, bd_stream_t stream);
 
+/* Natural NVFP4 B -> the E4M3-sideband tiled layout (regrouped only; read with BD_GEMM_B_E4M3).
+ * Same arguments and checks as bd_pack_b. The layout the reference-facing operator shim takes. */
+int bd_pack_b_e4m3(const uint8_t* codes, const uint8_t* scales16, uint8_t* codes_tiled,
+                   uint8_t* scales_tiled, int N, int K, bd_stream_t stream);
+
 /* Natural MXFP6 A (one code per byte, (M, K/32) E8M0) -> GEMM operand layout. K % 128 == 0.
  * scales_tiled must hold K/32 * Mp4 bytes; padding rows are written as 127 (2^0). The codes are
  * already in the operand layout: a_packed receives a copy with bits 6..7 cleared, and
@@ -195,8 +204,11 @@ int bd_w4a6_gemm(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8
 /* Launch flags of bd_w4a6_gemm_ex. */
 #define BD_GEMM_OVERLAP_PREV 1u   /* may start while the previous kernel on the stream ends */
 #define BD_GEMM_WEIGHTS_STATIC 2u /* b / b_scales are not written by that previous kernel */
+#define BD_GEMM_B_E4M3 4u         /* b / b_scales in the E4M3-sideband layout (bd_pack_b_e4m3) */
 
-/* bd_w4a6_gemm with launch flags (same arguments, same results).
+/* bd_w4a6_gemm with launch flags (same arguments, same results). BD_GEMM_B_E4M3: b and b_scales
+ * are in the E4M3-sideband layout (bd_pack_b_e4m3) instead of bd_pack_b's; same results for the
+ * same natural weights (the transcode then decodes the scale bytes on chip).
  * BD_GEMM_OVERLAP_PREV launches with programmatic stream serialisation: the kernel's CTAs may
  * be scheduled as the previous kernel's CTAs retire (the previous kernel must allow it:
  * bd_w4a6_gemm kernels do, other kernels start it only when they end). The kernel waits for

@@ -28,7 +28,7 @@ def lib():
 def test_header_declares_the_entry_points():
     fns = declared_functions()
     for f in ("bd_transcode_nvfp4_to_mxfp6", "bd_w4a6_gemm", "bd_w4a6_gemm_ex",
-              "bd_splitk_reduce", "bd_pack_b", "bd_pack_a", "bd_query_workspace"):
+              "bd_splitk_reduce", "bd_pack_b", "bd_pack_b_e4m3", "bd_pack_a", "bd_query_workspace"):
         assert f in fns
 
 
@@ -70,9 +70,9 @@ def test_gemm_ex_validates_flags_then_arguments(lib):
     ok = P(4096)
     g = lib.bd_w4a6_gemm_ex
     # unknown flag bit
-    assert g(ok, ok, ok, ok, ok, 1.0, None, 16, 128, 128, 1, 0, 0, 0, None, 0, 4, None) == -1
-    # known flags, then the same checks as bd_w4a6_gemm
-    assert g(None, ok, ok, ok, ok, 1.0, None, 16, 128, 128, 1, 0, 0, 0, None, 0, 3, None) == -1
+    assert g(ok, ok, ok, ok, ok, 1.0, None, 16, 128, 128, 1, 0, 0, 0, None, 0, 8, None) == -1
+    # known flags (BD_GEMM_B_E4M3 = 4 among them), then the same checks as bd_w4a6_gemm
+    assert g(None, ok, ok, ok, ok, 1.0, None, 16, 128, 128, 1, 0, 0, 0, None, 0, 7, None) == -1
     assert g(ok, ok, ok, ok, ok, 1.0, None, 16, 100, 128, 1, 0, 0, 0, None, 0, 1, None) == -2
 
 
@@ -92,6 +92,7 @@ def test_pack_rejects_bad_shapes(lib):
     P = ctypes.c_void_p
     ok = P(4096)
     assert lib.bd_pack_b(ok, ok, ok, ok, 100, 128, None) == -2
+    assert lib.bd_pack_b_e4m3(ok, ok, ok, ok, 100, 128, None) == -2
     assert lib.bd_pack_a(ok, ok, ok, ok, 4, 100, None) == -2
     assert lib.bd_splitk_reduce(ok, ok, None, 1.0, 4, 6, 2, 0, 0, None) == -2
 

@@ -337,3 +337,23 @@ def test_pack_activations_in_place_gives_the_same_gemm():
     assert packed.codes.data_ptr() == codes.data_ptr()
     got = bd.w4a6_gemm(packed, w)
     assert torch.equal(got, ref)
+
+
+@pytest.mark.parametrize("M,N,K,split_k", [(16, 2048, 4096, 0), (1, 14336, 1024, 0),
+                                           (128, 1024, 2048, 1), (300, 768, 1024, 2)])
+def test_both_weight_layouts_give_the_same_bytes(M, N, K, split_k):
+    """bd_pack_b's transcode-ready layout (moved sign bits, class words) and the E4M3 sideband
+    (bd_pack_b_e4m3, read with BD_GEMM_B_E4M3) produce the same B tile on chip, so the GEMM
+    results are identical; full-range scale bytes (subnormal and zero scales, large gaps)."""
+    import bitdance_b200 as bd
+    ops = random_operands(M, N, K, seed=M + N + K + split_k, b_scale_lo=0x00, b_scale_hi=0x7E)
+    acts = bd.pack_activations(dev(ops[0]), dev(ops[1]))
+    out = []
+    for sideband in ("class", "e4m3"):
+        w = bd.pack_weights(dev(ops[2]), dev(ops[3]), 0.5, sideband=sideband)
+        out.append(bd.w4a6_gemm(acts, w, split_k=split_k, out_dtype=torch.float32).clone())
+    torch.cuda.synchronize()
+    assert bd.device_error() == 0
+    assert torch.equal(out[0], out[1])
+    C, Cabs = gold(*ops, 0.5)
+    check(out[0], C, Cabs, torch.float32)

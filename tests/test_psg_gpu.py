@@ -33,20 +33,18 @@ def ref_buffers(M, N, K, dev="cuda"):
 @pytest.mark.parametrize("b_scale,b_byte", [(1.0, 0x38), (2.0, 0x40), (1.5, 0x3C)])
 def test_verify_w4a6_byte_uniform(a_val, a_byte, b_val, b_scale, b_byte):
     """verify_w4a6.py --dtype w6a6_tc --a_uniform_byte: expected = K*a_val*b_val*b_scale,
-    pass at |err| <= 1e-3*|expected| (:185-192)."""
+    pass at |err| <= 1e-3*|expected| (:185-192). The buffers are filled the way the script
+    fills them -- constant code and scale bytes straight into the reference-sized buffers, no
+    packer -- which the operator reads as the reference does."""
     from bitdance_b200.psg import compile_preshuffle_gemm_a8
     M, N, K = 128, 256, 2048
     sa, sb, bias, lut = ref_buffers(M, N, K)
     a = torch.full((M, K), a_byte, dtype=torch.uint8, device="cuda")
     bc = o.E2M1_POS.tolist().index(b_val)
     b_nat = torch.full((N, K // 2), (bc << 4) | bc, dtype=torch.uint8, device="cuda")
-    s_nat = torch.full((N, K // 16), b_byte, dtype=torch.uint8, device="cuda")
     sa.fill_(127)
-    import bitdance_b200 as bd
-    w = bd.pack_weights(b_nat, s_nat)
-    b = torch.zeros((N, K // 2), dtype=torch.uint8, device="cuda")
-    b.view(-1).copy_(w.codes)
-    sb[: w.scales.numel()].copy_(w.scales)
+    b = b_nat
+    sb.fill_(b_byte)
     c = torch.zeros((M, N), dtype=torch.bfloat16, device="cuda")
     launch = compile_preshuffle_gemm_a8(M=M, N=N, K=K, tile_m=128, tile_n=256, tile_k=128,
                                         in_dtype="w6a6_tc", out_dtype="bf16")
@@ -70,7 +68,7 @@ def _random_launch(M, N, K, split_k, split_reduce, seed=0):
     b_nat = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device="cuda", generator=g)
     s_nat = torch.randint(0x30, 0x48, (N, K // 16), dtype=torch.uint8, device="cuda", generator=g)
     acts = bd.pack_activations(a_nat, e8_nat)
-    w = bd.pack_weights(b_nat, s_nat)
+    w = bd.pack_weights(b_nat, s_nat, sideband="e4m3")
     sa[: acts.scales.numel()].copy_(acts.scales)
     sb[: w.scales.numel()].copy_(w.scales)
     if split_reduce == "atomic":
