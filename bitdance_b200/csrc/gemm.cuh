@@ -17,7 +17,8 @@
 //
 // Warp roles (736 threads):
 //   warp 0      weight producer  TMA: packed NVFP4 codes (2 x 8 KB per chunk, 64B-swizzled)
-//                                and E4M3 scales (2 x 1 KB) into the weight ring (deep).
+//                                and their scale sideband (2 x 1 KB: class words, or E4M3
+//                                bytes with BD_GEMM_B_E4M3) into the weight ring.
 //   warp 22     token producer   TMA: token rows (one E2M3 code per byte, 128B-swizzled) and
 //                                their E8M0 scales into the token ring.
 //   warps 6..21 transcode        two groups of 8 warps taking alternate chunks (two chunks in
@@ -119,6 +120,7 @@ struct GemmCfg {
                 "TMA shared-memory destinations 128-byte aligned");
   static_assert(SW <= 4 && SB <= 4 && ST <= 8, "control block sizes");
   static_assert(SW % kGroups == 0 && SB % kGroups == 0, "slots owned by one group");
+  static_assert(8 * kPermCopies == 64, "class words hold table rows times 64 bytes");
 };
 
 struct GemmCtl {
