@@ -2,7 +2,7 @@
 """Generate the golden fixtures in this directory by running the REFERENCE's own Python code
 (scimg/bitdance, read-only at REF_ROOT). Run in the build container only:
 
-    python tests/golden/make_golden.py [REF_ROOT]
+    python tests/golden/make_golden.py REF_ROOT     (or REF_ROOT in the environment)
 
 Nothing at test time reads the reference; the tests read the .npz/.json files written here.
 Every fixture records which reference function produced it.
@@ -17,7 +17,9 @@ import tempfile
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("REF_ROOT", "")
+if not REF or not os.path.isdir(REF):
+    sys.exit("usage: make_golden.py REF_ROOT (the reference checkout, read-only)")
 
 # The reference reads these at import (vector_quant_error.py:156-177); pin the defaults.
 os.environ["MXFP6_E4M3_SUBNORMAL"] = "0"
