@@ -138,6 +138,21 @@ def test_psg_shim_validation_matches_reference_errors():
     assert c(K=256, tile_m=128, tile_n=128, tile_k=128, in_dtype="w6a6_tc").K == 256
 
 
+def test_psg_launch_reads_weights_as_the_reference_bytes(monkeypatch):
+    """The drop-in launch passes BD_GEMM_B_E4M3: b / scale_b hold the reference's code and E4M3
+    scale bytes (only regrouped), so buffers filled the way kernel/verify_w4a6.py and
+    kernel/bench_sweep.py fill them mean the same. Checked on the call the shim makes."""
+    from bitdance_b200 import _lib, psg
+    seen = []
+    monkeypatch.setattr(psg, "call", lambda name, *args: seen.append((name, args)))
+    launch = psg.compile_preshuffle_gemm_a8(M=16, N=256, K=256, tile_m=128, tile_n=256,
+                                            tile_k=128, in_dtype="w4a6_tc", out_dtype="bf16")
+    launch(4096, 8192, 12288, 16384, 20480, 24576, 28672, 16, 256, None, b_tensor_scale=0.5)
+    (name, args), = seen
+    assert name == "bd_w4a6_gemm_ex"
+    assert args[-2] == _lib.BD_GEMM_B_E4M3 and args[5] == 0.5
+
+
 def test_product_path_never_imports_the_oracle():
     pkg = os.path.join(ROOT, "bitdance_b200")
     for dirpath, _, files in os.walk(pkg):
