@@ -369,6 +369,15 @@ __device__ __forceinline__ int last_segment(const Schedule& sch, int c, Seg& las
   return n;
 }
 
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
@@ -549,7 +558,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
     const int grp = tw / Cfg::kGroupWarps;
     constexpr int R = Cfg::kRowsPerThread;
     // rows of this thread: 32 (tw % group warps) + lane + 32 * group warps * r
-    int code_row[R], scale_off[R], b_row[R], sw[R], r7[R], rows[R];
+    int code_sw[R], scale_off[R], b_sw[R], rows[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int row = r * (32 * Cfg::kGroupWarps) + (tw % Cfg::kGroupWarps) * 32 + lane;
@@ -557,13 +566,14 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
       rows[r] = row;
       // raw codes: 64B-swizzled 128-row halves, 16-byte chunk c of row rr at
       // rr*64 + ((c ^ ((rr >> 1) & 3)) << 4); chunk c holds K block c
-      code_row[r] = (row >> 7) * 8192 + rr * 64;
-      sw[r] = (rr >> 1) & 3;
+      // the row offset has zero bits 4..5 and the stage base is 1 KB aligned, so the address
+      // of chunk c is (stage + row offset + swizzle << 4) ^ (c << 4)
+      code_sw[r] = (row >> 7) * 8192 + rr * 64 + (((rr >> 1) & 3) << 4);
       scale_off[r] = Cfg::kWCodes + (row >> 7) * 1024 + rr * 8;
       // B operand: 128B-swizzled K-major, 16-byte chunk cc of row n at
       // (n >> 3)*1024 + (n & 7)*128 + ((cc ^ (n & 7)) << 4); block b covers chunks 2b, 2b + 1
-      b_row[r] = (row >> 3) * 1024 + (row & 7) * 128;
-      r7[r] = row & 7;
+      // likewise bits 4..6: chunk cc of row n at (slot + row offset + ((n & 7) << 4)) ^ (cc << 4)
+      b_sw[r] = (row >> 3) * 1024 + (row & 7) * 128 + ((row & 7) << 4);
     }
     const uint8_t* perm = smem + Cfg::oPerm + (lane % Cfg::kPermCopies) * 8;
     int ci = 0;  // chunk number within this CTA
@@ -581,7 +591,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         for (int r = 0; r < R; ++r) {
 #pragma unroll
           for (int c = 0; c < 4; ++c)
-            q[r][c] = *reinterpret_cast<const uint4*>(st + code_row[r] + ((c ^ sw[r]) << 4));
+            q[r][c] = ld_shared_v4((smem_u32(st) + code_sw[r]) ^ (c << 4));
           sc[r] = *reinterpret_cast<const uint2*>(st + scale_off[r]);
         }
         // The weight stage is released only after the B rows computed from it are stored
@@ -630,8 +640,8 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
               nib8_natural_to_e4m3(q[r][blk].z, T1, v[4], v[5]);
               nib8_natural_to_e4m3(q[r][blk].w, T1, v[6], v[7]);
             }
-            st_shared_v4(bt + b_row[r] + (((2 * blk) ^ r7[r]) << 4), v[0], v[1], v[2], v[3]);
-            st_shared_v4(bt + b_row[r] + (((2 * blk + 1) ^ r7[r]) << 4), v[4], v[5], v[6], v[7]);
+            st_shared_v4((bt + b_sw[r]) ^ ((2 * blk) << 4), v[0], v[1], v[2], v[3]);
+            st_shared_v4((bt + b_sw[r]) ^ ((2 * blk + 1) << 4), v[4], v[5], v[6], v[7]);
           }
           // E8M0 bytes of the row's four 32-blocks (class words: bits 10..14 + 118)
           if constexpr (kClassWords)
