@@ -1,18 +1,29 @@
 #!/usr/bin/env python3
 """Benchmark of the W4A6 GEMM (MXFP6 activations x NVFP4 weights transcoded on chip).
 
-Workload (the decode sweep): N=14336, K=4096, M in {1,4,16,32,64}.
+Headline workload (the decode sweep): N=14336, K=4096, M in {1,4,16,32,64}.
 One step = for each M, one GEMM against each of L=8 distinct weight matrices (a decode pass
 over 8 layers), i.e. 40 GEMMs reading 8 x 33.0 MB of NVFP4 weights per M. The 8 matrices
-(264 MB) exceed the 126 MB L2, so every GEMM streams its weights from HBM.
+(264 MB) exceed the 126 MB L2, so every GEMM streams its weights from HBM. Weights: Student-t
+(df 5) scaled to std 0.02, NVFP4-quantised on the GPU; activations: N(0,1) with 0.1% of the K
+channels times 20, MXFP6-quantised on the GPU (seeds in the line's `data`).
 
 Metric: decode weight GB/s = weight bytes (N*K/2 codes + N*K/16 E4M3 scales + 4) per GEMM,
 summed over the step, divided by the step time. Multi-GPU (torchrun): every rank holds its own
-N-shard of a (14336*world) x 4096 weight matrix per layer and runs the same sweep with no
-collective in the timed region (weak scaling); the time is the max over ranks.
+14336-row N-shard of a (14336*world) x 4096 weight matrix per layer and runs the same sweep
+with no collective in the timed region (weak scaling); the time is the max over ranks.
 
---impl reference times the reference's CPU path (the oracle port of kernel/nvfp4_codec.py +
-dequantise + fp32 matmul) on the host cores instead.
+Also in the line:
+* `configs`: BASELINE configs 1, 3 and 4 on one GPU (time, TFLOP/s, weight GB/s, roofline
+  against the measured tensor peak of the MMA probe or the measured HBM copy rate);
+* `sharded_70b` (every N): config 4 (N=28672, K=8192, M in {16, 4096}) column-sharded across
+  the ranks (strong scaling): the sharded GEMM's time (max over ranks), the one-GPU time of the
+  whole matrix on rank 0, efficiency t1 / (N t_N), the NCCL all-gather of C timed on its own,
+  and a bit-for-bit check of the gathered C against per-shard GEMMs on rank 0;
+* `cpu_baseline`: the reference's CPU path (the oracle port of its codec + dequantise + fp32
+  matmul) on the host cores, transcode and GEMM timed separately.
+
+--impl reference times that CPU path instead (rank 0 only).
 
 Prints one JSON line (rank 0).
 """
@@ -21,6 +32,7 @@ from __future__ import annotations
 import argparse
 import datetime
 import json
+import math
 import os
 import statistics
 import sys
@@ -35,10 +47,19 @@ M_SWEEP = (1, 4, 16, 32, 64)
 LAYERS = 8
 METRIC = "decode weight GB/s (W4A6 GEMM, NVFP4 weights transcoded on chip)"
 UNIT = "GB/s"
+SEED_W, SEED_A = 2, 3            # decode sweep: weights layer l use SEED_W * 100 + l
+N70, K70 = 28672, 8192
+L2_BYTES = 126 * 2 ** 20
 
 
 def weight_bytes(N, K):
     return N * K // 2 + N * K // 16 + 4
+
+
+def alg_bytes(M, N, K):
+    """Algorithmic bytes of one GEMM: weights + A (one code byte + 1/32 scale byte per
+    element) + C (bf16)."""
+    return weight_bytes(N, K) + M * K + M * K // 32 + 2 * M * N
 
 
 def load_peaks():
@@ -62,7 +83,8 @@ def load_traffic():
 
 
 class ClockSampler(threading.Thread):
-    """Samples SM clock, max clock, power and clock-event reasons via NVML (read only)."""
+    """Samples SM clock, power and clock-event reasons via NVML (read only) while the timed
+    regions run (started before the first, stopped after the last)."""
 
     REASONS = {
         "sw_power_cap": 0x4, "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
@@ -70,11 +92,12 @@ class ClockSampler(threading.Thread):
         "applications_clocks_setting": 0x2,
     }
 
-    def __init__(self, index, period=0.01):
+    def __init__(self, index, period=0.002):
         super().__init__(daemon=True)
         self.index, self.period = index, period
         self.samples = []
         self.stop_evt = threading.Event()
+        self.active = threading.Event()
         self.ok = False
         try:
             import pynvml
@@ -88,13 +111,14 @@ class ClockSampler(threading.Thread):
 
     def run(self):
         while self.ok and not self.stop_evt.is_set():
-            try:
-                sm = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
-                rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                pw = self.nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
-                self.samples.append((sm, rs, pw))
-            except Exception:
-                pass
+            if self.active.is_set():
+                try:
+                    sm = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                    rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                    pw = self.nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+                    self.samples.append((sm, rs, pw))
+                except Exception:
+                    pass
             time.sleep(self.period)
 
     def summary(self):
@@ -117,13 +141,8 @@ class ClockSampler(threading.Thread):
 # ----------------------------------------------------------------------------------------
 # CPU leg: the reference's CPU path (oracle port), timed on the host cores.
 
-def cpu_reference_run(seconds=10.0, rows=512):
-    """Per GEMM of the sweep: NVFP4 -> MXFP6 transcode of a `rows`-row slice of the weights
-    (C restatement, all threads), dequantisation, fp32 matmul (OpenBLAS) with M tokens.
-    Returns (weight GB/s, cores, sample description)."""
+def _orc():
     import ctypes
-    import numpy as np
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
     lib_path = os.path.join(ROOT, "oracle", "liborc.so")
     if not os.path.exists(lib_path):
         import subprocess
@@ -134,32 +153,107 @@ def cpu_reference_run(seconds=10.0, rows=512):
                                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
     lib.orc_dequant.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
                                 ctypes.c_void_p, ctypes.c_int]
+    return lib
+
+
+def blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        info = [i for i in threadpool_info() if i.get("user_api") == "blas"]
+        if info:
+            return {"library": info[0].get("internal_api"), "version": info[0].get("version"),
+                    "threads": info[0].get("num_threads")}
+    except Exception:
+        pass
+    return None
+
+
+def cpu_reference_run(seconds=10.0, rows=512):
+    """Per GEMM of the decode sweep: NVFP4 -> MXFP6 transcode of a `rows`-row slice of the
+    weights (C restatement, all host threads), then the GEMM: dequantisation and an fp32 matmul
+    (OpenBLAS) with M tokens; the two parts are timed separately. Returns a dict with the
+    weight GB/s of the whole path and of each part, the seconds per GEMM of each part (scaled
+    to the full 14336-row matrix), the thread counts and the sample description."""
+    import numpy as np
+    lib = _orc()
     cores = os.cpu_count() or 1
-    rng = np.random.default_rng(2)
+    rng = np.random.default_rng(SEED_W)
     K = K_W
     packed = rng.integers(0, 256, (rows, K // 2), dtype=np.uint8)
-    scales = rng.integers(0x58, 0x7F, (rows, K // 16), dtype=np.uint8)
+    scales = rng.integers(0x28, 0x50, (rows, K // 16), dtype=np.uint8)
     nblk = rows * K // 32
     e6 = np.empty(nblk * 32, np.uint8)
     e8 = np.empty(nblk, np.uint8)
     Bf = np.empty((rows, K), np.float32)
     acts = {M: rng.standard_normal((M, K)).astype(np.float32) for M in M_SWEEP}
     done = 0
+    t_tx = t_mm = 0.0
     t0 = time.perf_counter()
     while True:
         for M in M_SWEEP:
+            a = time.perf_counter()
             lib.orc_transcode(packed.ctypes.data, scales.ctypes.data, nblk, 16, e6.ctypes.data,
                               e8.ctypes.data, cores)
+            b = time.perf_counter()
             lib.orc_dequant(e6.ctypes.data, e8.ctypes.data, nblk, Bf.ctypes.data, cores)
             _ = acts[M] @ Bf.T
+            c = time.perf_counter()
+            t_tx += b - a
+            t_mm += c - b
             done += 1
         el = time.perf_counter() - t0
         if el >= seconds:
             break
-    gbs = done * weight_bytes(rows, K) / el / 1e9
-    sample = (f"{done} GEMMs of the M sweep on a {rows}x{K} weight slice "
-              f"(transcode + dequant + fp32 matmul), {el:.1f} s")
-    return gbs, cores, sample
+    wb = weight_bytes(rows, K)
+    scale_full = N_W / rows
+    return {
+        "value": done * wb / (t_tx + t_mm) / 1e9,
+        "transcode_gbs": done * wb / t_tx / 1e9,
+        "gemm_gbs": done * wb / t_mm / 1e9,
+        "transcode_s_per_gemm": t_tx / done * scale_full,
+        "gemm_s_per_gemm": t_mm / done * scale_full,
+        "cores": cores,
+        "blas": blas_threads(),
+        "sample": (f"{done} GEMMs of the M sweep on a {rows}x{K} weight slice "
+                   f"(transcode {t_tx:.1f} s + dequant and fp32 matmul {t_mm:.1f} s), "
+                   f"{el:.1f} s; per-GEMM seconds scaled to N={N_W}"),
+    }
+
+
+def cpu_config_rates(seconds=4.0):
+    """Throughputs of the CPU path's two parts on representative shapes, for the per-config
+    table: transcode (weight bytes/s, C restatement, all threads) and dequant + fp32 matmul
+    (GEMM flop/s at M=128, K=4096, OpenBLAS). Per-config CPU seconds are these rates applied
+    to each config's bytes and flops (extrapolated; the full prefill matmul would take minutes)."""
+    import numpy as np
+    lib = _orc()
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(9)
+    rows, K, M = 1024, 4096, 128
+    packed = rng.integers(0, 256, (rows, K // 2), dtype=np.uint8)
+    scales = rng.integers(0x28, 0x50, (rows, K // 16), dtype=np.uint8)
+    nblk = rows * K // 32
+    e6 = np.empty(nblk * 32, np.uint8)
+    e8 = np.empty(nblk, np.uint8)
+    Bf = np.empty((rows, K), np.float32)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    t_tx = t_mm = 0.0
+    n = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        a = time.perf_counter()
+        lib.orc_transcode(packed.ctypes.data, scales.ctypes.data, nblk, 16, e6.ctypes.data,
+                          e8.ctypes.data, cores)
+        b = time.perf_counter()
+        lib.orc_dequant(e6.ctypes.data, e8.ctypes.data, nblk, Bf.ctypes.data, cores)
+        _ = A @ Bf.T
+        c = time.perf_counter()
+        t_tx += b - a
+        t_mm += c - b
+        n += 1
+    return {"transcode_bytes_per_s": n * weight_bytes(rows, K) / t_tx,
+            "gemm_flops_per_s": n * 2.0 * M * rows * K / t_mm,
+            "dequant_matmul_shape": f"M={M} x {rows}x{K}", "iterations": n}
 
 
 def run_reference(args, rank, world):
@@ -167,11 +261,12 @@ def run_reference(args, rank, world):
         return 0
     t_run = time.perf_counter()
     vals = []
+    last = None
     for _ in range(max(1, args.warmup)):
         cpu_reference_run(seconds=0.5)
     for _ in range(args.steps):
-        v, cores, sample = cpu_reference_run(seconds=max(0.25, args.cpu_seconds / max(1, args.steps)))
-        vals.append(v)
+        last = cpu_reference_run(seconds=max(0.25, args.cpu_seconds / max(1, args.steps)))
+        vals.append(last["value"])
     value = statistics.median(vals)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
@@ -179,8 +274,9 @@ def run_reference(args, rank, world):
         "scaling": "weak", "vs_baseline": None, "dtype": "u8 codes -> fp32", "data": "synthetic",
         "config": {"workload": f"decode sweep N={N_W} K={K_W} M in {list(M_SWEEP)}",
                    "path": "CPU oracle port of the reference codec + numpy fp32 matmul"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": last["cores"], "kind": "port",
+                         "sample": last["sample"], "blas": last["blas"],
+                         "transcode_gbs": last["transcode_gbs"], "gemm_gbs": last["gemm_gbs"]},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "wall_s": time.perf_counter() - t_run,
     }
@@ -189,7 +285,216 @@ def run_reference(args, rank, world):
 
 
 # ----------------------------------------------------------------------------------------
-# GPU leg
+# GPU leg: synthetic operands with the BASELINE configs' distributions
+
+def gen_student_t(torch, shape, std, g):
+    """Student-t (df 5) scaled to standard deviation `std`: z / sqrt(chi2_5 / 5)."""
+    z = torch.randn(shape, device=g.device, generator=g)
+    chi = torch.zeros(shape, device=g.device)
+    for _ in range(5):
+        chi += torch.randn(shape, device=g.device, generator=g).square()
+    return z / torch.sqrt(chi / 5.0) * (std / math.sqrt(5.0 / 3.0))
+
+
+def gen_outlier_acts(torch, shape, g):
+    """N(0,1) with 0.1% of the K channels multiplied by 20."""
+    x = torch.randn(shape, device=g.device, generator=g)
+    ch = torch.rand(shape[-1], device=g.device, generator=g) < 0.001
+    return torch.where(ch[None, :], x * 20.0, x)
+
+
+def generator(torch, dev, seed):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    return g
+
+
+def graph_of(torch, body, stream):
+    """CUDA graph of one call of `body` (warmed outside the graph first)."""
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        body()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            body()
+    return graph
+
+
+def time_graph(torch, graph, stream, iters, warmup=3):
+    """Mean ms per replay, CUDA events on the launching stream, synchronised on both sides."""
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(iters):
+            graph.replay()
+        t1.record(stream)
+    torch.cuda.synchronize()
+    return t0.elapsed_time(t1) / iters
+
+
+def rotating_copies(bytes_each, min_total=3 * L2_BYTES):
+    """How many distinct copies of an operand make the rotating working set exceed L2."""
+    return max(2, -(-min_total // max(1, bytes_each)))
+
+
+def clone_weights(ops, w):
+    return ops.PackedWeights(w.codes.clone(), w.scales.clone(), w.tensor_scale, w.N, w.K,
+                             w.sideband)
+
+
+def gemm_roofline(M, N, K, ms, tensor_peak, tensor_kind, hbm_peak, hbm_kind):
+    """One GEMM's figures and its roofline: the bound is the one whose time is longer at the
+    peaks (flops / tensor peak vs algorithmic bytes / HBM copy rate)."""
+    flops = 2.0 * M * N * K
+    ab = alg_bytes(M, N, K)
+    tflops = flops / (ms / 1e3) / 1e12
+    gbs = ab / (ms / 1e3) / 1e9
+    tensor_bound = flops / (tensor_peak * 1e12) >= ab / (hbm_peak * 1e9)
+    roof = ({"bound": "tensor", "achieved": tflops, "peak": tensor_peak, "unit": "TFLOP/s",
+             "frac": tflops / tensor_peak, "peak_kind": tensor_kind} if tensor_bound else
+            {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+             "frac": gbs / hbm_peak, "peak_kind": hbm_kind})
+    return {"M": M, "N": N, "K": K, "ms": ms, "us": ms * 1e3, "tflops": tflops,
+            "weight_gbs": weight_bytes(N, K) / (ms / 1e3) / 1e9, "alg_gbs": gbs,
+            "frac_of_tensor_peak": tflops / tensor_peak, "frac_of_hbm": gbs / hbm_peak,
+            "roofline": roof}
+
+
+def time_gemm_config(torch, ops, dev, M, N, K, w_kind, w_std, a_kind, seed, stream,
+                     launches=None):
+    """One BASELINE config on one GPU: weights quantised on the GPU from the config's
+    distribution, rotated over enough copies that the working set exceeds L2, the GEMMs of one
+    pass captured in a CUDA graph (back to back, programmatic serialisation with static
+    weights). Returns ms per GEMM."""
+    g = generator(torch, dev, seed)
+    w = (gen_student_t(torch, (N, K), w_std, g) if w_kind == "t"
+         else torch.randn((N, K), device=dev, generator=g) * w_std)
+    pw = ops.quantize_weights(w)
+    del w
+    x = gen_outlier_acts(torch, (M, K), g) if a_kind == "outlier" else \
+        torch.randn((M, K), device=dev, generator=g)
+    acts = ops.quantize_activations(x)
+    del x
+    reps = rotating_copies(weight_bytes(N, K))
+    ws = [pw] + [clone_weights(ops, pw) for _ in range(reps - 1)]
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    wsp = ops.Workspace()
+    n = launches or max(reps, 8)
+
+    def body():
+        for i in range(n):
+            ops.w4a6_gemm(acts, ws[i % reps], out=out, workspace=wsp, stream=stream,
+                          overlap_prev=True, weights_static=True)
+    graph = graph_of(torch, body, stream)
+    ms = time_graph(torch, graph, stream, iters=3) / n
+    del graph
+    return ms
+
+
+def sharded_70b(torch, ops, dev, rank, world, stream, steps):
+    """Config 4 column-sharded across the ranks (strong scaling) -- see the module doc."""
+    import torch.distributed as dist
+    from bitdance_b200 import shard
+    res = {"N": N70, "K": K70, "world": world, "shard_rows": N70 // world}
+    # every rank draws the whole matrix from the same seed, so the tensor scale is global, and
+    # quantises it on its own GPU; it keeps only its shard (rank 0 also keeps all, for the check)
+    g = generator(torch, dev, 4000)
+    w = torch.randn((N70, K70), device=dev, generator=g) * 0.015
+    codes, sc, tstat = ops.quantize_nvfp4(w)
+    del w
+    s_t = ops.tensor_scale_of(tstat)
+    lo, hi = shard.shard_rows(N70, world, rank)
+    mine = ops.pack_weights(codes[lo:hi].contiguous(), sc[lo:hi].contiguous(), s_t)
+    full = ops.pack_weights(codes, sc, s_t) if rank == 0 else None
+    per = {}
+    for M in (16, 4096):
+        ga = generator(torch, dev, 4100 + M)
+        acts = ops.quantize_activations(torch.randn((M, K70), device=dev, generator=ga))
+        n = hi - lo
+        reps = rotating_copies(weight_bytes(n, K70))
+        ws = [mine] + [clone_weights(ops, mine) for _ in range(reps - 1)]
+        out = torch.empty((M, n), dtype=torch.bfloat16, device=dev)
+        wsp = ops.Workspace()
+        launches = max(reps, 8)
+
+        def body():
+            for i in range(launches):
+                ops.w4a6_gemm(acts, ws[i % reps], out=out, workspace=wsp, stream=stream,
+                              overlap_prev=True, weights_static=True)
+        graph = graph_of(torch, body, stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = time_graph(torch, graph, stream, iters=max(3, steps // 20)) / launches
+        del graph, ws
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        entry = {"t_N_ms": ms, "weight_gbs_total": weight_bytes(N70, K70) / (ms / 1e3) / 1e9,
+                 "tflops_total": 2.0 * M * N70 * K70 / (ms / 1e3) / 1e12}
+        # the whole matrix on one GPU (rank 0), same method
+        if rank == 0:
+            entry["t_1_ms"] = time_gemm_full(torch, ops, acts, full, stream)
+            entry["efficiency"] = entry["t_1_ms"] / (world * ms)
+        if world > 1:
+            dist.barrier()
+            # all-gather of the bf16 shards over NCCL, timed on its own (not in t_N)
+            C = ops.w4a6_gemm(acts, mine, stream=torch.cuda.current_stream())
+            buf = torch.empty((world * M, n), dtype=C.dtype, device=dev)
+            for _ in range(3):
+                dist.all_gather_into_tensor(buf, C)
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            it = 10
+            e0.record()
+            for _ in range(it):
+                dist.all_gather_into_tensor(buf, C)
+            e1.record()
+            torch.cuda.synchronize()
+            ag = e0.elapsed_time(e1) / it
+            t = torch.tensor([ag], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ag = float(t.item())
+            recv = (world - 1) * M * n * 2
+            entry["allgather_ms"] = ag
+            entry["allgather_gbs_per_gpu"] = recv / (ag / 1e3) / 1e9
+            gathered = shard.assemble(buf.view(world, M, n))
+            if rank == 0:
+                # bit for bit against the per-shard GEMMs of rank 0 (same schedule per shard)
+                ref = torch.cat([ops.w4a6_gemm(acts, ops.pack_weights(
+                    codes[r * n:(r + 1) * n].contiguous(), sc[r * n:(r + 1) * n].contiguous(),
+                    s_t)) for r in range(world)], dim=1)
+                entry["gather_bit_exact"] = bool(torch.equal(gathered, ref))
+            dist.barrier()
+        per[f"M{M}"] = entry
+    res["per_M"] = per
+    return res
+
+
+def time_gemm_full(torch, ops, acts, full, stream):
+    reps = rotating_copies(weight_bytes(full.N, full.K))
+    ws = [full] + [clone_weights(ops, full) for _ in range(reps - 1)]
+    out = torch.empty((acts.M, full.N), dtype=torch.bfloat16, device=acts.codes.device)
+    wsp = ops.Workspace()
+    launches = max(reps, 8)
+
+    def body():
+        for i in range(launches):
+            ops.w4a6_gemm(acts, ws[i % reps], out=out, workspace=wsp, stream=stream,
+                          overlap_prev=True, weights_static=True)
+    graph = graph_of(torch, body, stream)
+    ms = time_graph(torch, graph, stream, iters=3) / launches
+    del graph, ws
+    return ms
+
 
 def run_ours(args, rank, world, local_rank):
     import torch
@@ -199,31 +504,29 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     bd.load()
-    g = torch.Generator(device=dev)
-    g.manual_seed(1234 + rank)
+    peaks, peak_kind = load_peaks()
 
-    def rand_u8(shape, lo, hi):
-        return torch.randint(lo, hi, shape, dtype=torch.uint8, device=dev, generator=g)
-
-    # weights: L layers of this rank's N-shard, NVFP4 bytes (values do not change the timing)
+    # weights: L layers of this rank's N-shard, Student-t, NVFP4-quantised on the GPU
     weights = []
-    for _ in range(LAYERS):
-        codes = rand_u8((N_W, K_W // 2), 0, 256)
-        sc = rand_u8((N_W, K_W // 16), 0x58, 0x7F)
-        weights.append(ops.pack_weights(codes, sc, 1.0 / 2688.0))
-        del codes, sc
-    # activations per M (natural codes + scales, packed once for the kernel-level leg)
-    nat = {M: (rand_u8((M, K_W), 0, 64), rand_u8((M, K_W // 32), 120, 135)) for M in M_SWEEP}
+    for layer in range(LAYERS):
+        g = generator(torch, dev, SEED_W * 100 + layer + 1000 * rank)
+        w = gen_student_t(torch, (N_W, K_W), 0.02, g)
+        weights.append(ops.quantize_weights(w))
+        del w
+    # activations per M: outlier channels, MXFP6-quantised on the GPU (natural codes + scales)
+    nat = {}
+    for M in M_SWEEP:
+        g = generator(torch, dev, SEED_A * 100 + M)
+        nat[M] = ops.quantize_mxfp6(gen_outlier_acts(torch, (M, K_W), g))
     acts = {M: ops.pack_activations(*nat[M]) for M in M_SWEEP}
     outs = {M: torch.empty((M, N_W), dtype=torch.bfloat16, device=dev) for M in M_SWEEP}
-    splits = {M: 0 for M in M_SWEEP}   # 0 = persistent stream-K schedule
     wss = {M: ops.Workspace() for M in M_SWEEP}
     launches_per_step = len(M_SWEEP) * LAYERS
 
     # no-output guard (kernel/bench_sweep.py:297-326): a launch must write C
     for M in M_SWEEP:
         outs[M].zero_()
-        ops.w4a6_gemm(acts[M], weights[0], out=outs[M], split_k=splits[M], workspace=wss[M])
+        ops.w4a6_gemm(acts[M], weights[0], out=outs[M], workspace=wss[M])
     torch.cuda.synchronize()
     if not all(bool(outs[M].any()) for M in M_SWEEP):
         raise RuntimeError("W4A6 GEMM wrote no output; refusing to time it")
@@ -238,7 +541,7 @@ def run_ours(args, rank, world, local_rank):
     def step_kernels():
         for M in M_SWEEP:
             for w in weights:
-                ops.w4a6_gemm(acts[M], w, out=outs[M], split_k=splits[M], workspace=wss[M],
+                ops.w4a6_gemm(acts[M], w, out=outs[M], workspace=wss[M],
                               stream=stream, overlap_prev=ov, weights_static=ov)
 
     # e2e: pinned host inputs -> device, pack (public API), GEMMs, device -> pinned host outputs
@@ -278,9 +581,8 @@ def run_ours(args, rank, world, local_rank):
         for M in e2e_order:
             cur.wait_event(ready[M])
             for w in weights:
-                ops.w4a6_gemm(e2e_acts[M], w, out=outs[M], split_k=splits[M],
-                              workspace=wss[M], stream=cur, overlap_prev=ov,
-                              weights_static=ov)
+                ops.w4a6_gemm(e2e_acts[M], w, out=outs[M], workspace=wss[M], stream=cur,
+                              overlap_prev=ov, weights_static=ov)
             done = torch.cuda.Event()
             done.record(cur)
             s_out.wait_event(done)
@@ -289,19 +591,13 @@ def run_ours(args, rank, world, local_rank):
         cur.wait_stream(s_in)
         cur.wait_stream(s_out)
 
-    def capture(fn):
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(stream):
-            fn()  # warm the allocator outside the graph
-            torch.cuda.synchronize()
-            with torch.cuda.graph(graph, stream=stream):
-                fn()
-        return graph
+    g_k = graph_of(torch, step_kernels, stream)
+    g_e = graph_of(torch, step_e2e, stream)
 
-    g_k = capture(step_kernels)
-    g_e = capture(step_e2e)
+    clocks = ClockSampler(local_rank)
+    clocks.start()
 
-    def timed(graph, steps, warmup, clocks=None):
+    def timed(graph, steps, warmup):
         with torch.cuda.stream(stream):
             for _ in range(warmup):
                 graph.replay()
@@ -309,8 +605,7 @@ def run_ours(args, rank, world, local_rank):
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
-        if clocks is not None:
-            clocks.start()
+        clocks.active.set()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
@@ -319,7 +614,7 @@ def run_ours(args, rank, world, local_rank):
                 graph.replay()
             t1.record(stream)
         torch.cuda.synchronize()
-        clk = clocks.summary() if clocks is not None else None
+        clocks.active.clear()
         if world > 1:
             torch.distributed.barrier()
         ms = t0.elapsed_time(t1)
@@ -327,15 +622,14 @@ def run_ours(args, rank, world, local_rank):
             tt = torch.tensor([ms], device=dev)
             torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
             ms = float(tt.item())
-        return ms, clk
+        return ms
 
-    clocks = ClockSampler(local_rank)
-    ms_k, clk = timed(g_k, args.steps, args.warmup, clocks)
-    ms_e, _ = timed(g_e, max(3, args.steps // 2), args.warmup)
+    ms_k = timed(g_k, args.steps, args.warmup)
     steps_e = max(3, args.steps // 2)
+    ms_e = timed(g_e, steps_e, args.warmup)
     # the host copies hold each batch's last-layer output: it must equal a fresh device GEMM
     for M in M_SWEEP:
-        ref = ops.w4a6_gemm(acts[M], weights[-1], split_k=splits[M]).cpu()
+        ref = ops.w4a6_gemm(acts[M], weights[-1]).cpu()
         if not torch.equal(ref, h_out[M]):
             raise RuntimeError(f"e2e output for M={M} differs from the device GEMM")
 
@@ -351,28 +645,78 @@ def run_ours(args, rank, world, local_rank):
     def step_dom():
         for M in dom_M:
             for w in weights:
-                ops.w4a6_gemm(acts[M], w, out=outs[M], split_k=splits[M], workspace=wss[M],
+                ops.w4a6_gemm(acts[M], w, out=outs[M], workspace=wss[M],
                               stream=stream, overlap_prev=ov, weights_static=ov)
-    g_d = capture(step_dom)
-    ms_d, _ = timed(g_d, args.steps, args.warmup)
+    g_d = graph_of(torch, step_dom, stream)
+    ms_d = timed(g_d, args.steps, args.warmup)
     n_dom = len(dom_M) * LAYERS
-    alg_dom = [weight_bytes(N_W, K_W) + M * K_W + M * K_W // 32 + 2 * M * N_W for M in dom_M]
-    alg_per_launch = sum(alg_dom) / len(alg_dom)
+    alg_per_launch = sum(alg_bytes(M, N_W, K_W) for M in dom_M) / len(dom_M)
     us_per_launch = ms_d * 1e3 / (args.steps * n_dom)
-    peaks, peak_kind = load_peaks()
     achieved = alg_per_launch / (us_per_launch * 1e-6) / 1e9
     tpw = load_traffic()
-    del g_d
+    # per-M GEMM time of the sweep (one graph per M, the same launches as the step)
+    per_m = {}
+    for M in M_SWEEP:
+        def step_m(M=M):
+            for w in weights:
+                ops.w4a6_gemm(acts[M], w, out=outs[M], workspace=wss[M],
+                              stream=stream, overlap_prev=ov, weights_static=ov)
+        gm = graph_of(torch, step_m, stream)
+        clocks.active.set()
+        us = time_graph(torch, gm, stream, iters=max(3, args.steps // 4)) * 1e3 / LAYERS
+        clocks.active.clear()
+        per_m[str(M)] = {"us": us, "weight_gbs": weight_bytes(N_W, K_W) / us / 1e3,
+                         "frac_of_hbm": weight_bytes(N_W, K_W) / us / 1e3 / peaks["hbm_gbs"]}
+        del gm
+    del g_d, g_k, g_e
+
+    # tensor peak of the block-scaled MMA, measured now (SS and TS operand forms)
+    probe = None
+    tensor_peak, tensor_kind = 2.0 * peaks["bf16_tflops"], "2x measured cuBLAS bf16 burst"
+    if not args.no_configs:
+        try:
+            ss = ops.mma_peak_tflops(n_cols=256, a_from_tmem=False)
+            ts = ops.mma_peak_tflops(n_cols=256, a_from_tmem=True)
+            probe = {"ss_tflops": ss, "ts_tflops": ts,
+                     "what": "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale M=128 N=256 "
+                             "K=32, one CTA per SM, back to back (bd_probe_mma_peak)"}
+            tensor_peak, tensor_kind = max(ss, ts), "measured by the MMA probe (this run)"
+        except Exception as e:  # noqa: BLE001 - report, keep the fallback
+            probe = {"error": repr(e)}
 
     extra = {}
-    if not args.no_prefill and world == 1:
-        extra["prefill"] = prefill_bench(torch, ops, dev, g, peaks)
+    if world == 1 and not args.no_configs:
+        cfgs = {}
+        clocks.active.set()
+        cases = {
+            "1": (128, 4096, 4096, "normal", 0.02, "normal", 10),
+            "3_gate_up": (8192, 14336, 4096, "t", 0.02, "outlier", 30),
+            "3_down": (8192, 4096, 14336, "t", 0.02, "outlier", 31),
+            "4_M16": (16, N70, K70, "normal", 0.015, "normal", 40),
+            "4_M4096": (4096, N70, K70, "normal", 0.015, "normal", 41),
+        }
+        for name, (M, N, K, wk, ws_, ak, seed) in cases.items():
+            ms = time_gemm_config(torch, ops, dev, M, N, K, wk, ws_, ak, seed, stream)
+            cfgs[name] = gemm_roofline(M, N, K, ms, tensor_peak, tensor_kind,
+                                       peaks["hbm_gbs"], peak_kind)
+        clocks.active.clear()
+        extra["configs"] = cfgs
+    if not args.no_sharded:
+        clocks.active.set()
+        extra["sharded_70b"] = sharded_70b(torch, ops, dev, rank, world, stream, args.steps)
+        clocks.active.clear()
+    clk = clocks.summary()
+    if bd.device_error() != 0:
+        raise RuntimeError("kernel error word set")
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_k / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "mxfp6 x mxfp6 (fp32 accumulate, bf16 out)",
-        "data": "synthetic (uniform random E2M1 codes and E4M3 scale bytes; timing is value-independent)",
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "mxfp6 x mxfp6 (fp32 accumulate, bf16 out)",
+        "data": (f"synthetic: weights Student-t(df 5) std 0.02 -> NVFP4 on the GPU (torch "
+                 f"generator seeds {SEED_W * 100}+layer), activations N(0,1) with 0.1% of "
+                 f"channels x20 -> MXFP6 on the GPU (seeds {SEED_A * 100}+M)"),
         "config": {"workload": f"decode sweep N={N_W} K={K_W} M in {list(M_SWEEP)} x {LAYERS} layers",
                    "per_rank_N": N_W, "global_N": N_W * world, "K": K_W,
                    "schedule": "persistent stream-K (tiles split across CTAs finished in-kernel)",
@@ -382,6 +726,7 @@ def run_ours(args, rank, world, local_rank):
                    "launch": "CUDA graph of one step" + (
                        ", programmatic serialisation between GEMMs" if ov else "")},
         "tflops": flops_step * args.steps / (ms_k / 1e3) / 1e12 * world,
+        "per_M": per_m,
         "roofline": {"bound": "hbm", "kernel": "w4a6_gemm_kernel<16> (launches with M = 1, 4, 16)",
                      "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "peak_kind": peak_kind,
@@ -392,61 +737,37 @@ def run_ours(args, rank, world, local_rank):
                              "kernel's mean launch duration (CUDA events over a graph of its "
                              "launches); traffic = DRAM bytes per launch from the committed ncu "
                              "summary (profiles/w4a6_gemm_decode.md)"},
+        "tensor_peak_probe": probe,
         "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "pinned host A -> device, bd_pack_a, bd_w4a6_gemm x layers, C -> pinned host"},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk,
         **extra,
     }
-    del g_k, g_e
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, sample = cpu_reference_run(seconds=args.cpu_seconds)
-        line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
-                                "sample": sample}
+        cpu = cpu_reference_run(seconds=args.cpu_seconds)
+        line["cpu_baseline"] = {"value": cpu["value"], "unit": UNIT, "cores": cpu["cores"],
+                                "kind": "port", "sample": cpu["sample"], "blas": cpu["blas"],
+                                "transcode_gbs": cpu["transcode_gbs"], "gemm_gbs": cpu["gemm_gbs"],
+                                "transcode_s_per_gemm": cpu["transcode_s_per_gemm"],
+                                "gemm_s_per_gemm": cpu["gemm_s_per_gemm"]}
+        if "configs" in line:
+            rates = cpu_config_rates()
+            line["cpu_baseline"]["config_rates"] = rates
+            for c in line["configs"].values():
+                c["cpu_transcode_s"] = weight_bytes(c["N"], c["K"]) / rates["transcode_bytes_per_s"]
+                c["cpu_gemm_s"] = 2.0 * c["M"] * c["N"] * c["K"] / rates["gemm_flops_per_s"]
     if rank == 0:
         print(json.dumps(line), flush=True)
     return 0
 
 
-def prefill_bench(torch, ops, dev, g, peaks):
-    """BASELINE config 3 shapes at M=8192 (gate/up 14336x4096, down 4096x14336): TFLOPS."""
-    res = {}
-    for name, (N, K) in {"gate_up": (14336, 4096), "down": (4096, 14336)}.items():
-        M = 8192
-        w = ops.pack_weights(torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev,
-                                           generator=g),
-                             torch.randint(0x58, 0x7F, (N, K // 16), dtype=torch.uint8, device=dev,
-                                           generator=g), 1.0)
-        a = ops.pack_activations(torch.randint(0, 64, (M, K), dtype=torch.uint8, device=dev,
-                                               generator=g),
-                                 torch.randint(120, 135, (M, K // 32), dtype=torch.uint8,
-                                               device=dev, generator=g))
-        out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-        wsp = ops.Workspace()
-        for _ in range(3):
-            ops.w4a6_gemm(a, w, out=out, workspace=wsp)
-        torch.cuda.synchronize()
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        it = 10
-        t0.record()
-        for _ in range(it):
-            ops.w4a6_gemm(a, w, out=out, workspace=wsp)
-        t1.record()
-        torch.cuda.synchronize()
-        ms = t0.elapsed_time(t1) / it
-        tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
-        res[name] = {"M": M, "N": N, "K": K, "ms": ms, "tflops": tf,
-                     "frac_of_2x_bf16_peak": tf / (2.0 * peaks["bf16_tflops"])}
-    return res
-
-
 def run_case(args):
     """One kernel shape, repeated: `--case gemm` (a single W4A6 GEMM), `--case transcode`
     (the standalone NVFP4 -> MXFP6 transcode of config 5), `--case quantize` (the MXFP6
-    activation quantiser) or `--case quantize_b` (the NVFP4 weight quantiser; bytes count the
-    two passes over the weights). Prints its own JSON line; used for Nsight Compute captures of one
-    launch."""
+    activation quantiser), `--case quantize_b` (the NVFP4 weight quantiser; bytes count the
+    two passes over the weights) or `--case probe` (the tensor-core MMA probe). Prints its own
+    JSON line; used for Nsight Compute captures of one launch."""
     import torch
     import bitdance_b200 as bd
     from bitdance_b200 import ops
@@ -454,20 +775,33 @@ def run_case(args):
     torch.cuda.set_device(dev)
     g = torch.Generator(device=dev)
     g.manual_seed(7)
+    if args.case == "probe":
+        res = {"case": "probe"}
+        for n in (64, 128, 256):
+            for tm in (False, True):
+                res[f"N{n}_{'ts' if tm else 'ss'}_tflops"] = ops.mma_peak_tflops(
+                    n_cols=n, a_from_tmem=tm, mmas_per_cta=args.steps * 64)
+        print(json.dumps(res), flush=True)
+        return 0
     if args.case == "gemm":
         # weight matrices rotate so the working set exceeds the 126 MB L2; the calls are
         # captured in one CUDA graph so the time is device time, not host launch overhead
         M, N, K = args.M, args.N, args.K
         reps = max(2, -(-300_000_000 // weight_bytes(N, K)))
-        ws_list = [ops.pack_weights(torch.randint(0, 256, (N, K // 2), dtype=torch.uint8,
-                                                  device=dev, generator=g),
-                                    torch.randint(0x58, 0x7F, (N, K // 16), dtype=torch.uint8,
-                                                  device=dev, generator=g), 1.0)
-                   for _ in range(reps)]
-        a = ops.pack_activations(torch.randint(0, 64, (M, K), dtype=torch.uint8, device=dev,
-                                               generator=g),
-                                 torch.randint(120, 135, (M, K // 32), dtype=torch.uint8,
-                                               device=dev, generator=g))
+        if args.dist == "t":
+            base = ops.quantize_weights(gen_student_t(torch, (N, K), 0.02, g))
+            ws_list = [base] + [clone_weights(ops, base) for _ in range(reps - 1)]
+            a = ops.quantize_activations(gen_outlier_acts(torch, (M, K), g))
+        else:
+            ws_list = [ops.pack_weights(torch.randint(0, 256, (N, K // 2), dtype=torch.uint8,
+                                                      device=dev, generator=g),
+                                        torch.randint(0x58, 0x7F, (N, K // 16), dtype=torch.uint8,
+                                                      device=dev, generator=g), 1.0)
+                       for _ in range(reps)]
+            a = ops.pack_activations(torch.randint(0, 64, (M, K), dtype=torch.uint8, device=dev,
+                                                   generator=g),
+                                     torch.randint(120, 135, (M, K // 32), dtype=torch.uint8,
+                                                   device=dev, generator=g))
         out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
         split = args.split
         wsp = ops.Workspace()
@@ -487,7 +821,7 @@ def run_case(args):
         fn = graph.replay  # noqa: E731
         calls = args.steps
         work = {"M": M, "N": N, "K": K, "split_k": split, "overlap": ov, "rotating_weights": reps,
-                "weight_bytes": weight_bytes(N, K), "flops": 2 * M * N * K}
+                "dist": args.dist, "weight_bytes": weight_bytes(N, K), "flops": 2 * M * N * K}
     elif args.case == "linear":
         # raw bf16 activations -> on-device quantiser -> GEMM (w4a6_linear), over rotating
         # weight matrices, captured in one CUDA graph
@@ -562,14 +896,14 @@ def run_case(args):
         fn = lambda: ops.transcode(codes, sc, 16, e2m3=e6, e8m0=e8)  # noqa: E731
         calls = 1
         work = {"nblk32": nblk, "bytes": nblk * (16 + 2 + 32 + 1)}
+    graphed = args.case in ("gemm", "linear", "quantize", "quantize_b")
     with torch.cuda.stream(stream):
-        for _ in range(max(3, args.warmup if args.case not in ("gemm", "linear", "quantize",
-                                                               "quantize_b") else 3)):
+        for _ in range(3 if graphed else max(3, args.warmup)):
             fn()
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    reps_t = 3 if args.case in ("gemm", "linear", "quantize", "quantize_b") else args.steps
+    reps_t = 3 if graphed else args.steps
     with torch.cuda.stream(stream):
         t0.record(stream)
         for _ in range(reps_t):
@@ -591,13 +925,17 @@ def run_case(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", choices=["gemm", "linear", "transcode", "quantize", "quantize_b"],
+    ap.add_argument("--case", choices=["gemm", "linear", "transcode", "quantize", "quantize_b",
+                                       "probe"],
                     default=None,
                     help="time one kernel shape instead of the benchmark step")
     ap.add_argument("--M", type=int, default=16)
     ap.add_argument("--N", type=int, default=14336)
     ap.add_argument("--K", type=int, default=4096)
     ap.add_argument("--split", type=int, default=0)
+    ap.add_argument("--dist", choices=["bytes", "t"], default="bytes",
+                    help="--case gemm operands: uniform random bytes, or config-2 distributions "
+                         "(Student-t weights, outlier activations) quantised on the GPU")
     ap.add_argument("--overlap", type=int, default=1,
                     help="--case gemm: launch with programmatic serialisation (weights static)")
     ap.add_argument("--nblk", type=int, default=1 << 26)
@@ -609,10 +947,16 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the per-config figures (configs 1, 3, 4) and the MMA probe")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the config-4 sharded (strong scaling) figures")
+    ap.add_argument("--no-prefill", action="store_true", help="alias of --no-configs")
     ap.add_argument("--no-overlap", action="store_true",
                     help="launch every GEMM only after the previous kernel completed")
     args = ap.parse_args()
+    if args.no_prefill:
+        args.no_configs = True
     if args.warmup < 3:
         args.warmup = 3
     if args.case:

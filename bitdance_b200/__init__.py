@@ -6,6 +6,7 @@ is its Python host side. ``psg`` mirrors the reference operator ``compile_preshu
 """
 from ._lib import BitdanceError, load  # noqa: F401
 from .ops import (PackedActivations, PackedWeights, Workspace, device_error,  # noqa: F401
+                  mma_peak_tflops,
                   pack_activations, pack_weights, quantize_activations, quantize_mxfp6,
                   quantize_nvfp4, quantize_weights, query_workspace, tensor_scale_of,
                   transcode, w4a6_gemm, w4a6_gemm_noalloc, w4a6_linear)

@@ -27,7 +27,7 @@ BD_EPI_NONE, BD_EPI_BIAS, BD_EPI_BIAS_RELU, BD_EPI_BIAS_SILU, BD_EPI_BIAS_GELU =
 BD_SPLIT_REDUCE, BD_SPLIT_PLANES, BD_SPLIT_ATOMIC = 0, 1, 2
 BD_GEMM_OVERLAP_PREV, BD_GEMM_WEIGHTS_STATIC, BD_GEMM_B_E4M3 = 1, 2, 4
 BD_IN_F32, BD_IN_BF16 = 0, 1
-BD_DEVERR_WAIT_MASK, BD_DEVERR_WAIT_TMA, BD_DEVERR_NONFINITE = 0x1F, 0x01, 0x20
+BD_DEVERR_WAIT_MASK, BD_DEVERR_WAIT_TMA, BD_DEVERR_NONFINITE, BD_DEVERR_RANGE = 0x1F, 0x01, 0x20, 0x40
 
 # name -> (restype, argtypes); mirrors include/bitdance_b200.h
 _P = ctypes.c_void_p
@@ -40,10 +40,12 @@ SIGNATURES = {
     "bd_status_string": (ctypes.c_char_p, [_I]),
     "bd_device_error": (_I, [ctypes.POINTER(ctypes.c_uint32), _I]),
     "bd_selftest_bounded_wait": (_I, [_I64, _P]),
+    "bd_probe_mma_peak": (_I, [_I64, _I, _I, _P]),
     "bd_transcode_nvfp4_to_mxfp6": (_I, [_P, _P, _P, _P, _I64, _I, _P]),
     "bd_pack_b": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "bd_pack_b_e4m3": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "bd_pack_a": (_I, [_P, _P, _P, _P, _I, _I, _P]),
+    "bd_scales_e8m0_to_e4m3_pairs": (_I, [_P, _P, _I64, _P]),
     "bd_quantize_a_mxfp6": (_I, [_P, _I, _P, _P, _P, _I, _I, _P]),
     "bd_quantize_b_nvfp4": (_I, [_P, _I, _P, _P, _P, _I, _I, _P]),
     "bd_quantize_a_mxfp6_ex": (_I, [_P, _I, _P, _P, _P, _I, _I, ctypes.c_uint, _P]),

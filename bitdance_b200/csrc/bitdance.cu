@@ -11,6 +11,7 @@
 
 #include "../../include/bitdance_b200.h"
 #include "gemm.cuh"
+#include "probe.cuh"
 #include "quantize_b.cuh"
 #include "sm100.cuh"
 #include "transcode.cuh"
@@ -285,6 +286,27 @@ int bd_selftest_bounded_wait(int64_t limit_cycles, bd_stream_t stream) {
   return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
 }
 
+int bd_probe_mma_peak(int64_t mmas_per_cta, int n_cols, int a_from_tmem, bd_stream_t stream) {
+  if (mmas_per_cta < 1 || mmas_per_cta > (int64_t{1} << 21)) return BD_ERR_INVALID_ARG;
+  if (n_cols < 16 || n_cols > 256 || n_cols % 16) return BD_ERR_INVALID_ARG;
+  DeviceInfo* d = nullptr;
+  int st = device_info(&d);
+  if (st != BD_OK) return st;
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    if (cudaFuncSetAttribute(mma_peak_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kProbeSmem) != cudaSuccess)
+      return BD_ERR_CUDA;
+    configured.fetch_or(bit);
+  }
+  mma_peak_kernel<<<d->sm_count, 128, kProbeSmem, as_stream(stream)>>>(
+      static_cast<long long>(mmas_per_cta), n_cols, a_from_tmem ? 1 : 0, d->err);
+  return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
+}
+
 int bd_transcode_nvfp4_to_mxfp6(const uint8_t* codes, const uint8_t* scales, uint8_t* e2m3_out,
                                 uint8_t* e8m0_out, int64_t nblk32, int scale_block,
                                 bd_stream_t stream) {
@@ -337,6 +359,20 @@ int bd_pack_b(const uint8_t* codes, const uint8_t* scales16, uint8_t* codes_tile
 int bd_pack_b_e4m3(const uint8_t* codes, const uint8_t* scales16, uint8_t* codes_tiled,
                    uint8_t* scales_tiled, int N, int K, bd_stream_t stream) {
   return pack_b(codes, scales16, codes_tiled, scales_tiled, N, K, false, stream);
+}
+
+int bd_scales_e8m0_to_e4m3_pairs(const uint8_t* e8m0, uint8_t* e4m3_pairs, int64_t nblk32,
+                                  bd_stream_t stream) {
+  if (nblk32 < 0) return BD_ERR_SHAPE;
+  if (nblk32 == 0) return BD_OK;
+  if (!e8m0 || !e4m3_pairs) return BD_ERR_INVALID_ARG;
+  if (!aligned(e4m3_pairs, 2)) return BD_ERR_ALIGNMENT;
+  DeviceInfo* d = nullptr;
+  int st = device_info(&d);
+  if (st != BD_OK) return st;
+  e8m0_to_e4m3_pairs_kernel<<<grid_for(nblk32, 256, d), 256, 0, as_stream(stream)>>>(
+      e8m0, reinterpret_cast<uint16_t*>(e4m3_pairs), nblk32, d->err);
+  return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
 }
 
 int bd_pack_a(const uint8_t* codes, const uint8_t* e8m0, uint8_t* a_packed, uint8_t* scales_tiled,

@@ -20,6 +20,7 @@ enum : uint32_t {
   kErrWaitAccum = 1u << 3,   // epilogue gave up waiting for the accumulator
   kErrWaitMma = 1u << 4,     // transcode gave up waiting for the MMA to free a buffer
   kErrNonFinite = 1u << 5,   // the activation quantiser saw a NaN or an infinity
+  kErrRange = 1u << 6,       // a scale had no representation in the target format
   kErrShape = 1u << 8,       // the kernel saw a shape it does not support
 };
 

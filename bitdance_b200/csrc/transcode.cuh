@@ -300,6 +300,32 @@ __global__ void pack_b_kernel(const uint8_t* __restrict__ codes, const uint8_t* 
 }
 
 // Natural A codes (one per byte) -> 12+4 packed chunks; one thread per 16-element chunk.
+// MXFP4 weight scales -> the E4M3 sideband: E8M0 byte e of a 32-block becomes, for both of
+// its 16-blocks, the E4M3 byte of the same power of two 2^(e - 127) (normal for exponents
+// -6..8, subnormal 0x04 / 0x02 / 0x01 for -7 / -8 / -9). With a power-of-two E4M3 scale the
+// pair rule reproduces the MXFP4 block exactly (mantissa bits 0: no bump, codes = the E2M1
+// magnitudes, E8M0 = e), so an MXFP4 weight (the reference's "w4a6" arm: E2M1 codes with E8M0
+// per-32 scales) runs through the NVFP4 GEMM unchanged. Exponents outside -9..8 have no E4M3
+// form: the block's scale becomes 0 and kErrRange is raised in the error word.
+__global__ void e8m0_to_e4m3_pairs_kernel(const uint8_t* __restrict__ e8m0,
+                                          uint16_t* __restrict__ pairs, int64_t n,
+                                          uint32_t* err) {
+  bool bad = false;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int s = static_cast<int>(e8m0[i]) - 127;
+    uint32_t b;
+    if (s >= -6 && s <= 8) b = static_cast<uint32_t>(s + 7) << 3;
+    else if (s >= -9) b = 0x04u >> (-7 - s);  // -7, -8, -9: subnormal 2^-7, 2^-8, 2^-9
+    else {
+      b = 0u;
+      bad = true;
+    }
+    pairs[i] = static_cast<uint16_t>(b | (b << 8));
+  }
+  if (bad) atomicOr(err, kErrRange);
+}
+
 __global__ void pack_a_codes_kernel(const uint8_t* __restrict__ codes, uint8_t* __restrict__ out,
                                     int64_t nchunks) {
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nchunks;

@@ -34,9 +34,21 @@ def _stream(stream=None):
     return ctypes.c_void_p(s)
 
 
+def _check_device(t, what: str):
+    """The C ABI launches on the CURRENT device and builds its tensor maps, error word and
+    static scratch for it: a tensor on another device would be read through the wrong
+    context (an illegal-address fault) -- refuse it before the call."""
+    cur = torch.cuda.current_device()
+    idx = t.device.index if t.device.index is not None else cur
+    if idx != cur:
+        raise ValueError(f"{what} is on cuda:{idx} but the current device is cuda:{cur}; "
+                         "call inside `with torch.cuda.device(...)`")
+
+
 def _need(t: torch.Tensor, dtype, what: str, numel: Optional[int] = None):
     if not isinstance(t, torch.Tensor) or not t.is_cuda:
         raise TypeError(f"{what} must be a CUDA tensor")
+    _check_device(t, what)
     if t.dtype != dtype:
         raise TypeError(f"{what} must be {dtype}, got {t.dtype}")
     if not t.is_contiguous():
@@ -202,25 +214,55 @@ def query_workspace(M: int, N: int, K: int, split_k: int = 0, split_mode: str = 
     return int(_lib.load().bd_query_workspace(M, N, K, split_k, SPLIT_MODES[split_mode]))
 
 
+# Incremented whenever device_error() finds a bounded wait that ran out: a GEMM that gave up
+# mid-call can leave stream-K arrival counters set, so every Workspace re-zeroes before its
+# next use.
+_ws_epoch = 0
+
+
+def _note_device_error(word: int) -> None:
+    global _ws_epoch
+    if word & _lib.BD_DEVERR_WAIT_MASK:
+        _ws_epoch += 1
+
+
 class Workspace:
-    """Device scratch for bd_w4a6_gemm. Zeroed when allocated and whenever the problem shape
-    changes; between calls of one shape the stream-K counters are left at zero by the kernel
-    itself, so repeated calls (and CUDA-graph replays) need no clearing. One per stream."""
+    """Device scratch for bd_w4a6_gemm. Zeroed when allocated, whenever the problem shape
+    changes, and after device_error() reported a bounded wait that ran out (an aborted call
+    can leave its stream-K counters set); between calls of one shape the counters are left at
+    zero by the kernel itself, so repeated calls (and CUDA-graph replays) need no clearing.
+    The zeroing is ordered on the stream the GEMM runs on. One per stream."""
 
     def __init__(self, device=None):
         self.buf = None
         self.device = device
         self.key = None
+        self.epoch = _ws_epoch
 
-    def get(self, nbytes: int, device, key=None) -> Optional[torch.Tensor]:
+    def get(self, nbytes: int, device, key=None, stream=None) -> Optional[torch.Tensor]:
         if nbytes == 0:
             return None
-        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != device:
-            self.buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
-        elif key != self.key:
-            self.buf[:nbytes].zero_()
+        device = torch.device(device)
+        if device.type == "cuda" and stream is not None and not hasattr(stream, "cuda_stream"):
+            stream = torch.cuda.ExternalStream(int(stream), device=device)
+        ctx = torch.cuda.stream(stream) if (device.type == "cuda" and stream is not None) \
+            else _nullctx()
+        with ctx:
+            if self.buf is None or self.buf.numel() < nbytes or self.buf.device != device:
+                self.buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+            elif key != self.key or self.epoch != _ws_epoch:
+                self.buf[:nbytes].zero_()
         self.key = key
+        self.epoch = _ws_epoch
         return self.buf
+
+
+class _nullctx:
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *a):
+        return False
 
 
 _default_ws = {}
@@ -258,10 +300,10 @@ def w4a6_gemm(acts: PackedActivations, weights: PackedWeights,
     ws_bytes = query_workspace(M, N, K, split_k, split_mode)
     key = (M, N, K, split_k, split_mode)
     if isinstance(workspace, Workspace):
-        workspace = workspace.get(ws_bytes, acts.codes.device, key)
+        workspace = workspace.get(ws_bytes, acts.codes.device, key, stream)
     elif workspace is None and ws_bytes:
         workspace = _workspace_for(acts.codes.device, stream).get(ws_bytes, acts.codes.device,
-                                                                  key)
+                                                                  key, stream)
     if bias is not None:
         _need(bias, torch.bfloat16, "bias", N)
     epi = EPILOGUES[epilogue]
@@ -316,11 +358,40 @@ def w4a6_gemm_noalloc(acts: PackedActivations, weights: PackedWeights, out: torc
     return out
 
 
+def mma_peak_tflops(n_cols: int = 256, a_from_tmem: bool = False, mmas_per_cta: int = 1 << 16,
+                    reps: int = 3, stream=None) -> float:
+    """Measured rate of the block-scaled tensor-core MMA the GEMM uses (bd_probe_mma_peak):
+    one CTA per SM issuing mmas_per_cta back-to-back tcgen05.mma.kind::mxf8f6f4 of
+    M = 128, N = n_cols, K = 32, timed with CUDA events on the launching stream after one
+    warm-up launch; the best of `reps` launches, in TFLOP/s. The FP6 (= FP8-rate) denominator
+    of the GEMM's tensor roofline."""
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    args = (int(mmas_per_cta), int(n_cols), 1 if a_from_tmem else 0, _stream(stream))
+    call("bd_probe_mma_peak", *args)
+    best = None
+    for _ in range(max(1, reps)):
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        call("bd_probe_mma_peak", *args)
+        t1.record(stream)
+        t1.synchronize()
+        ms = t0.elapsed_time(t1)
+        best = ms if best is None else min(best, ms)
+    if device_error(clear=True) != 0:
+        raise RuntimeError("the MMA peak probe reported a device error")
+    flops = sms * float(mmas_per_cta) * 2.0 * 128 * n_cols * 32
+    return flops / (best / 1e3) / 1e12
+
+
 def device_error(clear: bool = True) -> int:
     """Error word set by the library's kernels (0 = none): bits 0..4 a bounded wait of the
     GEMM ran out, BD_DEVERR_NONFINITE (0x20) the quantiser saw NaN / Inf."""
     w = ctypes.c_uint32(0)
     call("bd_device_error", ctypes.byref(w), 1 if clear else 0)
+    _note_device_error(int(w.value))
     return int(w.value)
 
 

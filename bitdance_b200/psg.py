@@ -20,15 +20,23 @@ with the reference's argument order and meaning:
   (``ops.w4a6_gemm`` with ``ops.pack_weights``' default layout is the faster native path: the
   packer does the weight-only part of the transcode once.)
 * arg_bias: N bf16; arg_lut: accepted and ignored (the transcode tables are compiled into
-  the kernel); M, N: ints; stream: a torch stream, a raw handle or None.
+  the kernel); M, N: ints; stream: a torch stream, a raw handle or None (torch's current
+  stream).
+
+``in_dtype="w4a6"`` (the reference's MXFP6 x MXFP4 arm, psg_preshuffle_gemm.py:411-423, which
+kernel/verify_w4a6.py:166-172 uses as its bit-exact cross-check) takes arg_scale_b as one E8M0
+byte per 32-block (N*K/32 bytes, in the block order of the E4M3 sideband); each becomes the
+E4M3 byte pair of the same power of two (bd_scales_e8m0_to_e4m3_pairs), for which the NVFP4
+transcode reproduces the MXFP4 block exactly, and the same GEMM runs. E8M0 exponents outside
+[-9, 8] have no E4M3 form (BD_DEVERR_RANGE).
 
 Pointers may be torch tensors, ints, or objects with ``.value`` / ``.data_ptr()``. The
 per-tensor fp32 scale of the NVFP4 weights, which the reference signature has no slot for,
 is the keyword ``b_tensor_scale`` (default 1.0).
 
 Errors follow the reference: ValueError for an unknown dtype, out_dtype, split_k or
-split_reduce combination; NotImplementedError for dtypes outside the W4A6 transcode path and
-for tile_k != 128.
+split_reduce combination; NotImplementedError for dtypes outside the W4A6 family
+(w4a6_tc / w6a6_tc / w4a6) and for tile_k != 128.
 """
 from __future__ import annotations
 
@@ -56,8 +64,10 @@ def _addr(x) -> Optional[int]:
 
 
 def _stream(stream):
+    # like the reference scripts (kernel/bench_sweep.py:292), None means torch's current stream
     if stream is None:
-        return None
+        import torch
+        stream = torch.cuda.current_stream()
     if hasattr(stream, "cuda_stream"):
         return ctypes.c_void_p(stream.cuda_stream)
     return ctypes.c_void_p(int(stream))
@@ -66,14 +76,30 @@ def _stream(stream):
 class W4A6Launcher:
     """The compiled operator: call it like the reference's launch_fn."""
 
-    def __init__(self, K, split_k, split_reduce, out_dtype, epilogue, tiles):
+    def __init__(self, K, split_k, split_reduce, out_dtype, epilogue, tiles, in_dtype="w4a6_tc"):
         self.K = K
         self.split_k = split_k
         self.split_reduce = split_reduce
         self.out_dtype = out_dtype
         self.epilogue = epilogue
         self.tiles = tiles
+        self.in_dtype = in_dtype
         self._ws = {}
+        self._pairs = {}   # (device, bytes) -> E4M3 scale pairs of the "w4a6" arm
+
+    def _mxfp4_scales(self, arg_scale_b, N, stream):
+        """The "w4a6" arm's E8M0 weight scales (one byte per 32-block, in the order of the
+        E4M3 sideband's blocks) as E4M3 byte pairs of the same powers of two."""
+        import torch
+        nblk = N * self.K // 32
+        dev = torch.cuda.current_device()
+        key = (dev, nblk)
+        if key not in self._pairs:
+            self._pairs[key] = torch.empty(2 * nblk, dtype=torch.uint8, device="cuda")
+        buf = self._pairs[key]
+        call("bd_scales_e8m0_to_e4m3_pairs", ctypes.c_void_p(_addr(arg_scale_b)),
+             ctypes.c_void_p(buf.data_ptr()), nblk, stream)
+        return buf.data_ptr()
 
     def workspace_bytes(self, M, N):
         return 0  # planes / atomic / split_k=1 need none
@@ -87,11 +113,15 @@ class W4A6Launcher:
             out = _lib.BD_OUT_F32
         epi = _EPI[self.epilogue]
         bias = _addr(arg_bias) if epi != _lib.BD_EPI_NONE else None
+        s = _stream(stream)
+        scale_b = _addr(arg_scale_b)
+        if self.in_dtype == "w4a6":
+            scale_b = self._mxfp4_scales(arg_scale_b, N, s)
         call("bd_w4a6_gemm_ex", ctypes.c_void_p(_addr(arg_c)), ctypes.c_void_p(_addr(arg_a)),
              ctypes.c_void_p(_addr(arg_scale_a)), ctypes.c_void_p(_addr(arg_b)),
-             ctypes.c_void_p(_addr(arg_scale_b)), float(b_tensor_scale),
+             ctypes.c_void_p(scale_b), float(b_tensor_scale),
              None if bias is None else ctypes.c_void_p(bias), M, N, self.K, self.split_k, mode,
-             out, epi, None, 0, _lib.BD_GEMM_B_E4M3, _stream(stream))
+             out, epi, None, 0, _lib.BD_GEMM_B_E4M3, s)
 
 
 @functools.lru_cache(maxsize=1024)
@@ -111,7 +141,7 @@ def compile_preshuffle_gemm_a8(*, M: int = 0, N: int = 0, K: int, tile_m: int, t
     round ties to even and are not bit-exact to the transcode table (psg:39-49)."""
     if in_dtype not in KNOWN_DTYPES:
         raise ValueError(f"in_dtype must be one of {KNOWN_DTYPES}, got {in_dtype!r}")
-    if in_dtype not in ("w4a6_tc", "w6a6_tc"):
+    if in_dtype not in ("w4a6_tc", "w6a6_tc", "w4a6"):
         raise NotImplementedError(
             f"in_dtype={in_dtype!r} is not the W4A6 transcode path this library implements")
     if out_dtype not in ("fp16", "bf16"):
@@ -145,4 +175,4 @@ def compile_preshuffle_gemm_a8(*, M: int = 0, N: int = 0, K: int, tile_m: int, t
         raise ValueError("a bias/activation epilogue needs the full sum; use split_k=1")
     _lib.load()
     return W4A6Launcher(int(K), split_k, split_reduce, out_dtype, epilogue,
-                        (int(tile_m), int(tile_n), int(tile_k)))
+                        (int(tile_m), int(tile_n), int(tile_k)), in_dtype)

@@ -87,6 +87,7 @@ const char* bd_status_string(int status);
 #define BD_DEVERR_WAIT_MASK 0x1Fu  /* a bounded wait of the GEMM ran out (bits 0..4)     */
 #define BD_DEVERR_WAIT_TMA 0x01u   /*   ... a consumer's wait for a TMA stage            */
 #define BD_DEVERR_NONFINITE 0x20u  /* a quantiser saw a NaN or an infinity               */
+#define BD_DEVERR_RANGE 0x40u      /* a scale had no form in the target format          */
 
 /* Reads (and, if clear != 0, resets) the error word that kernels of this library set on
  * the current device: a bounded wait that ran out, non-finite quantiser input. Synchronises
@@ -100,6 +101,15 @@ int bd_device_error(uint32_t* word, int clear);
  * second leaves through that flag. The kernel ends, the context stays usable, and the host
  * reads the status with bd_device_error. 1000 <= limit_cycles <= 4e9. */
 int bd_selftest_bounded_wait(int64_t limit_cycles, bd_stream_t stream);
+
+/* Tensor-core peak probe (the FP6 = FP8-rate roofline of the GEMM): one CTA per SM, each
+ * issuing mmas_per_cta block-scaled tcgen05.mma.kind::mxf8f6f4 (M = 128, N = n_cols, K = 32,
+ * E2M3 x E4M3 operands, E8M0 scales) back to back into one fp32 accumulator, operands on chip;
+ * A from shared memory (a_from_tmem == 0) or tensor memory (the GEMM's form). The caller times
+ * the launch on `stream`: rate = SMs * mmas_per_cta * 2 * 128 * n_cols * 32 / time.
+ * 1 <= mmas_per_cta <= 2^21; n_cols a multiple of 16 in [16, 256].
+ * Replaces the reference's MFMA issue-rate probe (kernel/hip/mfma_peak.hip:22-59). */
+int bd_probe_mma_peak(int64_t mmas_per_cta, int n_cols, int a_from_tmem, bd_stream_t stream);
 
 /* NVFP4 -> MXFP6 transcode, global -> global, natural layouts.
  * nblk32 blocks of 32 elements: codes 16 B per block, scales 2 B per block (scale_block 16,
@@ -122,6 +132,17 @@ int bd_pack_b(const uint8_t* codes, const uint8_t* scales16, uint8_t* codes_tile
  * Same arguments and checks as bd_pack_b. The layout the reference-facing operator shim takes. */
 int bd_pack_b_e4m3(const uint8_t* codes, const uint8_t* scales16, uint8_t* codes_tiled,
                    uint8_t* scales_tiled, int N, int K, bd_stream_t stream);
+
+/* MXFP4 weight scales (one E8M0 byte per 32-block) -> E4M3 scale bytes for both 16-blocks of
+ * each block (2 * nblk32 bytes out, in the same order): E8M0 e becomes the E4M3 byte of the
+ * power of two 2^(e-127), for which the per-16 pair rule reproduces the MXFP4 block exactly.
+ * Turns an MXFP4 weight (E2M1 codes, E8M0 per-32 scales: the reference's in_dtype="w4a6" arm,
+ * psg_preshuffle_gemm.py:411-423, the bit-exact cross-check of kernel/verify_w4a6.py:166-172)
+ * into NVFP4 bytes the GEMM takes. Exponents e - 127 outside [-9, 8] have no E4M3 form: those
+ * blocks get scale 0 and BD_DEVERR_RANGE is set in the device error word. e4m3_pairs 2-byte
+ * aligned. */
+int bd_scales_e8m0_to_e4m3_pairs(const uint8_t* e8m0, uint8_t* e4m3_pairs, int64_t nblk32,
+                                  bd_stream_t stream);
 
 /* Natural MXFP6 A (one code per byte, (M, K/32) E8M0) -> GEMM operand layout. K % 128 == 0.
  * scales_tiled must hold K/32 * Mp4 bytes; padding rows are written as 127 (2^0). The codes are

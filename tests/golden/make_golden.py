@@ -69,7 +69,9 @@ def pair_rule_ref(scale16: np.ndarray, codes: np.ndarray):
 
 
 def main():
-    meta = {"reference": REF, "env": {"MXFP6_E4M3_SUBNORMAL": "0", "MXFP6_E4M3_LEGACY_BOOK": "0"}}
+    # the project the fixtures come from, not the checkout path of the machine that made them
+    meta = {"reference": "scimg/bitdance",
+            "env": {"MXFP6_E4M3_SUBNORMAL": "0", "MXFP6_E4M3_LEGACY_BOOK": "0"}}
 
     # 1. LUTs: derived by transcode_lut.build_luts and the literal header.
     hdr = header_tables()

@@ -76,6 +76,17 @@ def test_gemm_ex_validates_flags_then_arguments(lib):
     assert g(ok, ok, ok, ok, ok, 1.0, None, 16, 100, 128, 1, 0, 0, 0, None, 0, 1, None) == -2
 
 
+def test_probe_and_scale_conversion_reject_bad_arguments(lib):
+    assert lib.bd_probe_mma_peak(0, 256, 0, None) == -1
+    assert lib.bd_probe_mma_peak(1 << 22, 256, 0, None) == -1
+    assert lib.bd_probe_mma_peak(1024, 24, 0, None) == -1
+    assert lib.bd_probe_mma_peak(1024, 272, 1, None) == -1
+    assert lib.bd_scales_e8m0_to_e4m3_pairs(None, None, -1, None) == -2
+    assert lib.bd_scales_e8m0_to_e4m3_pairs(None, None, 0, None) == 0
+    assert lib.bd_scales_e8m0_to_e4m3_pairs(None, None, 16, None) == -1
+    assert lib.bd_scales_e8m0_to_e4m3_pairs(8, 9, 16, None) == -3
+
+
 def test_transcode_rejects_bad_arguments(lib):
     P = ctypes.c_void_p
     ok = P(4096)
@@ -136,6 +147,10 @@ def test_psg_shim_validation_matches_reference_errors():
         c(K=256, tile_m=128, tile_n=128, tile_k=128, in_dtype="w4a6_tc", use_hw_transcode=True)
     # the alias resolves like the reference's (psg:341-342)
     assert c(K=256, tile_m=128, tile_n=128, tile_k=128, in_dtype="w6a6_tc").K == 256
+    # the MXFP4-weight arm the reference's verify script cross-checks against (psg:411-423)
+    assert c(K=256, tile_m=128, tile_n=128, tile_k=128, in_dtype="w4a6").in_dtype == "w4a6"
+    with pytest.raises(NotImplementedError):
+        c(K=256, tile_m=128, tile_n=128, tile_k=256, in_dtype="w4a6")
 
 
 def test_psg_launch_reads_weights_as_the_reference_bytes(monkeypatch):
@@ -147,7 +162,7 @@ def test_psg_launch_reads_weights_as_the_reference_bytes(monkeypatch):
     monkeypatch.setattr(psg, "call", lambda name, *args: seen.append((name, args)))
     launch = psg.compile_preshuffle_gemm_a8(M=16, N=256, K=256, tile_m=128, tile_n=256,
                                             tile_k=128, in_dtype="w4a6_tc", out_dtype="bf16")
-    launch(4096, 8192, 12288, 16384, 20480, 24576, 28672, 16, 256, None, b_tensor_scale=0.5)
+    launch(4096, 8192, 12288, 16384, 20480, 24576, 28672, 16, 256, 0, b_tensor_scale=0.5)
     (name, args), = seen
     assert name == "bd_w4a6_gemm_ex"
     assert args[-2] == _lib.BD_GEMM_B_E4M3 and args[5] == 0.5

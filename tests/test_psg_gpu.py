@@ -102,3 +102,79 @@ def test_split_k_matches_unsplit():
     a, gold = _random_launch(64, 256, 4096, 1, "atomic", seed=3)
     b, _ = _random_launch(64, 256, 4096, 8, "atomic", seed=3)
     assert np.abs(a - b).max() <= 1e-5 * np.abs(gold).max()
+
+
+def _e4m3_of_e8m0(e):
+    s = int(e) - 127
+    if -6 <= s <= 8:
+        return (s + 7) << 3
+    if -9 <= s <= -7:
+        return 0x04 >> (-7 - s)
+    return 0
+
+
+def test_e8m0_to_e4m3_pairs_every_byte():
+    """bd_scales_e8m0_to_e4m3_pairs over all 256 E8M0 bytes: the E4M3 byte of the same power of
+    two, duplicated for both 16-blocks; bytes without an E4M3 form give 0 and BD_DEVERR_RANGE."""
+    import bitdance_b200 as bd
+    from bitdance_b200 import _lib
+    from bitdance_b200._lib import call
+    assert bd.device_error() == 0
+    e8 = torch.arange(256, dtype=torch.uint8, device="cuda")
+    out = torch.full((512,), 0xEE, dtype=torch.uint8, device="cuda")
+    call("bd_scales_e8m0_to_e4m3_pairs", e8.data_ptr(), out.data_ptr(), 256, None)
+    got = out.cpu().numpy().reshape(256, 2)
+    want = np.array([_e4m3_of_e8m0(e) for e in range(256)], np.uint8)
+    assert np.array_equal(got[:, 0], want) and np.array_equal(got[:, 1], want)
+    assert bd.device_error() == _lib.BD_DEVERR_RANGE
+    # in range only: no error
+    call("bd_scales_e8m0_to_e4m3_pairs", e8[118:136].data_ptr(), out.data_ptr(), 18, None)
+    assert bd.device_error() == 0
+
+
+@pytest.mark.parametrize("split_k,split_reduce", [(1, "planes"), (4, "atomic")])
+def test_w4a6_arm_is_bit_exact_with_the_transcode_arm(split_k, split_reduce):
+    """kernel/verify_w4a6.py:166-172: with power-of-two weight scales, the MXFP4 arm ("w4a6",
+    E8M0 per-32 scales) and the NVFP4 transcode arm ("w6a6_tc", the same powers of two as E4M3
+    bytes) give bit-identical C; both match the MXFP4 gold (E2M1 x 2^(e-127))."""
+    from bitdance_b200.psg import compile_preshuffle_gemm_a8
+    import bitdance_b200 as bd
+    M, N, K = 64, 512, 2048
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11)
+    a_nat = torch.randint(0, 64, (M, K), dtype=torch.uint8, device="cuda", generator=g)
+    a_e8 = torch.randint(122, 132, (M, K // 32), dtype=torch.uint8, device="cuda", generator=g)
+    b_nat = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device="cuda", generator=g)
+    e8 = torch.randint(118, 136, (N, K // 32), dtype=torch.uint8, device="cuda", generator=g)
+    acts = bd.pack_activations(a_nat, a_e8)
+    # the NVFP4 form of the same weights: both 16-blocks carry the power of two as E4M3
+    lut = torch.tensor([_e4m3_of_e8m0(e) for e in range(256)], dtype=torch.uint8, device="cuda")
+    s16 = lut[e8.long()].repeat_interleave(2, dim=1).contiguous()
+    w = bd.pack_weights(b_nat, s16, sideband="e4m3")
+    # the MXFP4 arm's scale buffer: one E8M0 byte per 32-block, in the sideband's block order
+    # (the E8M0 bytes regrouped by the same packer, taking the first byte of each pair)
+    w8 = bd.pack_weights(b_nat, e8.repeat_interleave(2, dim=1).contiguous(), sideband="e4m3")
+    tiled_e8 = w8.scales.view(-1, 2)[:, 0].contiguous()
+    outs = {}
+    for dtype, sb in (("w6a6_tc", w.scales), ("w4a6", tiled_e8)):
+        launch = compile_preshuffle_gemm_a8(M=M, N=N, K=K, tile_m=128, tile_n=256, tile_k=128,
+                                            in_dtype=dtype, out_dtype="bf16", split_k=split_k,
+                                            split_reduce=split_reduce)
+        if split_reduce == "atomic":
+            c = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+        else:
+            c = torch.zeros((split_k, M, N), dtype=torch.bfloat16, device="cuda")
+        launch(c, acts.codes, w.codes, acts.scales, sb, None, None, M, N, None)
+        torch.cuda.synchronize()
+        outs[dtype] = c
+    assert bd.device_error() == 0
+    assert torch.equal(outs["w6a6_tc"], outs["w4a6"])
+    # gold: MXFP4 weights dequantised directly
+    codes = o.unpack_nibbles(b_nat.cpu().numpy()).astype(np.int64)
+    wv = np.where(codes & 8, -1.0, 1.0) * o.E2M1_POS[codes & 7]
+    wv *= np.repeat(np.exp2(e8.cpu().numpy().astype(np.float64) - 127), 32, axis=1)
+    av = o.dequant_operand(a_nat.cpu().numpy(), a_e8.cpu().numpy())
+    gold = av @ wv.T
+    got = outs["w4a6"].float()
+    got = (got.sum(0) if got.dim() == 3 else got).cpu().numpy()
+    assert o.rel_linf(gold, got) <= 1e-2
