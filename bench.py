@@ -670,6 +670,12 @@ def run_ours(args, rank, world, local_rank):
         del gm
     del g_d, g_k, g_e
 
+    def no_device_error(stage):
+        w = bd.device_error()
+        if w != 0:
+            raise RuntimeError(f"kernel error word 0x{w:x} set after {stage}")
+
+    no_device_error("the decode sweep")
     # tensor peak of the block-scaled MMA, measured now (SS and TS operand forms)
     probe = None
     tensor_peak, tensor_kind = 2.0 * peaks["bf16_tflops"], "2x measured cuBLAS bf16 burst"
@@ -699,15 +705,15 @@ def run_ours(args, rank, world, local_rank):
             ms = time_gemm_config(torch, ops, dev, M, N, K, wk, ws_, ak, seed, stream)
             cfgs[name] = gemm_roofline(M, N, K, ms, tensor_peak, tensor_kind,
                                        peaks["hbm_gbs"], peak_kind)
+            no_device_error(f"config {name}")
         clocks.active.clear()
         extra["configs"] = cfgs
     if not args.no_sharded:
         clocks.active.set()
         extra["sharded_70b"] = sharded_70b(torch, ops, dev, rank, world, stream, args.steps)
         clocks.active.clear()
+        no_device_error("the sharded config-4 GEMMs")
     clk = clocks.summary()
-    if bd.device_error() != 0:
-        raise RuntimeError("kernel error word set")
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,

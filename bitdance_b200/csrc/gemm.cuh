@@ -61,8 +61,8 @@ struct RingDepths {
   int sw, sb, st, groups;
 };
 constexpr RingDepths ring_depths(int BM) {
-  if (BM <= 16) return {4, 4, 8, 2};
-  if (BM <= 32) return {4, 4, 4, 2};
+  if (BM <= 16) return {4, 4, 6, 2};
+  if (BM <= 32) return {4, 4, 3, 2};
   if (BM <= 64) return {4, 2, 6, 2};
   return {4, 2, 4, 2};
 }
@@ -89,9 +89,10 @@ struct GemmCfg {
   static constexpr int oW = ST * kTRowBytes;
   static constexpr int oB = oW + SW * kWStage;
   static constexpr int oSf = oB + SB * kBStage;  // SB x 256 E8M0 words staged for tensor memory
-  // magnitude table, 8 copies interleaved (entry e of copy j at e*64 + j*8): lane l reads
-  // copy l % 8
-  static constexpr int kPermCopies = 8;  // a table row is 64 bytes: class words index it
+  // magnitude table, 16 copies interleaved (entry e of copy j at e*128 + j*8): copy j sits in
+  // bank pair j whatever the row, lane l reads copy l % 16, so the 8-byte lookups of a warp
+  // take the minimum two shared-memory wavefronts (two lanes per bank pair)
+  static constexpr int kPermCopies = 16;  // a table row is 128 bytes: class words index it
   static constexpr int oPerm = oSf + SB * 1024;
   static constexpr int oTs = oPerm + 64 * 8 * kPermCopies;  // token scale ring
   static constexpr int oCtl = oTs + ST * kTScaleSlot;
@@ -120,7 +121,7 @@ struct GemmCfg {
                 "TMA shared-memory destinations 128-byte aligned");
   static_assert(SW <= 4 && SB <= 4 && ST <= 8, "control block sizes");
   static_assert(SW % kGroups == 0 && SB % kGroups == 0, "slots owned by one group");
-  static_assert(8 * kPermCopies == 64, "class words hold table rows times 64 bytes");
+  static_assert(8 * kPermCopies == 128, "table rows are 128 bytes apart (class-word shifts)");
 };
 
 struct GemmCtl {
@@ -614,8 +615,8 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
             const uint32_t f = blk < 2 ? (sc[r].x >> (16 * blk)) : (sc[r].y >> (16 * (blk - 2)));
             uint32_t off0, off1;  // byte offsets of the two 16-blocks' table rows
             if constexpr (kClassWords) {
-              // class word: both rows times 64 (the byte stride of a row in the 8-copy table)
-              const uint32_t off_small = (f << 6) & 0xFC0u, off_big = f & 0x1C0u;
+              // class word: both rows times 128 (the byte stride of a row in the 16-copy table)
+              const uint32_t off_small = (f << 7) & 0x1F80u, off_big = (f << 1) & 0x380u;
               const bool first_big = (f & 0x200u) != 0;
               off0 = first_big ? off_big : off_small;
               off1 = first_big ? off_small : off_big;
@@ -675,7 +676,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
     const int quarter = warp & 3;
     const int ep_tid = tid - 64;  // 0..127
     const int mrow = quarter * 32 + lane;  // token row of the tile (accumulator lane)
-    constexpr int kEB = 16;                // accumulator columns per tensor-memory load
+    constexpr int kEB = 32;                // accumulator columns per tensor-memory load
     grid_dep_wait();  // C, bias and the workspace belong to the previous grid until it ends
     const uint32_t taddr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
     Seg lastseg;
@@ -753,7 +754,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
           for (int c0 = 0; c0 < ncols; c0 += kEB) {
             uint32_t r[kEB];
             __syncwarp();
-            tmem_ld_x16(taddr + c0, r);
+            tmem_ld_x32(taddr + c0, r);
             tmem_ld_wait();
             if (row_ok) {
               float4* dst = reinterpret_cast<float4*>(slot + mrow * kTileN + c0);
@@ -799,7 +800,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         for (int c0 = 0; c0 < ncols; c0 += kEB) {
           uint32_t r[kEB];
           __syncwarp();
-          tmem_ld_x16(taddr + c0, r);
+          tmem_ld_x32(taddr + c0, r);
           tmem_ld_wait();
           if (!row_ok) continue;  // the warp meets again at the next __syncwarp
           float acc[kEB];

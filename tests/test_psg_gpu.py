@@ -132,11 +132,12 @@ def test_e8m0_to_e4m3_pairs_every_byte():
     assert bd.device_error() == 0
 
 
-@pytest.mark.parametrize("split_k,split_reduce", [(1, "planes"), (4, "atomic")])
+@pytest.mark.parametrize("split_k,split_reduce", [(1, "planes"), (4, "planes"), (4, "atomic")])
 def test_w4a6_arm_is_bit_exact_with_the_transcode_arm(split_k, split_reduce):
     """kernel/verify_w4a6.py:166-172: with power-of-two weight scales, the MXFP4 arm ("w4a6",
     E8M0 per-32 scales) and the NVFP4 transcode arm ("w6a6_tc", the same powers of two as E4M3
-    bytes) give bit-identical C; both match the MXFP4 gold (E2M1 x 2^(e-127))."""
+    bytes) give bit-identical C (fp32 atomics add partials in no fixed order, so that mode is
+    compared within the tolerance); both match the MXFP4 gold (E2M1 x 2^(e-127))."""
     from bitdance_b200.psg import compile_preshuffle_gemm_a8
     import bitdance_b200 as bd
     M, N, K = 64, 512, 2048
@@ -168,7 +169,11 @@ def test_w4a6_arm_is_bit_exact_with_the_transcode_arm(split_k, split_reduce):
         torch.cuda.synchronize()
         outs[dtype] = c
     assert bd.device_error() == 0
-    assert torch.equal(outs["w6a6_tc"], outs["w4a6"])
+    if split_reduce == "atomic":
+        diff = (outs["w6a6_tc"] - outs["w4a6"]).abs().max().item()
+        assert diff <= 1e-5 * outs["w6a6_tc"].abs().max().item()
+    else:
+        assert torch.equal(outs["w6a6_tc"], outs["w4a6"])
     # gold: MXFP4 weights dequantised directly
     codes = o.unpack_nibbles(b_nat.cpu().numpy()).astype(np.int64)
     wv = np.where(codes & 8, -1.0, 1.0) * o.E2M1_POS[codes & 7]
