@@ -310,7 +310,10 @@ def generator(torch, dev, seed):
 
 
 def graph_of(torch, body, stream):
-    """CUDA graph of one call of `body` (warmed outside the graph first)."""
+    """CUDA graph of one call of `body` (warmed outside the graph first). Everything enqueued
+    before (on any stream) completes first: the operands were made on the default stream, and
+    buffers freed there may be reused by tensors the side stream writes."""
+    torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
         body()

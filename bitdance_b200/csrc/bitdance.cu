@@ -240,6 +240,17 @@ int launch_gemm_any(int bm, bool class_words, const GemmMaps& m, const GemmParam
                      : launch_gemm_bm<false>(bm, m, p, grid, overlap, s);
 }
 
+// The stream-K fix-up grid of 64- and 128-row token tiles (GemmParams::fixup_kernel), after the
+// GEMM on the same stream.
+int launch_fixup(int bm, const GemmParams& p, int64_t tiles, int gemm_grid, cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>(tiles * kFixupBlocks));
+  if (bm == 64)
+    streamk_fixup_kernel<64><<<grid, kFixupThreads, 0, s>>>(p, gemm_grid);
+  else
+    streamk_fixup_kernel<128><<<grid, kFixupThreads, 0, s>>>(p, gemm_grid);
+  return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
+}
+
 }  // namespace
 }  // namespace bd
 
@@ -612,6 +623,9 @@ int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const ui
   p.out_dtype = out_dtype;
   p.epilogue = epilogue;
   p.weights_early = (flags & BD_GEMM_WEIGHTS_STATIC) ? 1 : 0;
+  // 64- and 128-row tiles: partials of 32-128 KB per contributor are summed by a grid of their
+  // own (many SMs) instead of by each tile's last contributor (one SM)
+  p.fixup_kernel = (streamk && bm >= 64) ? 1 : 0;
   p.vec_out = aligned(c, 16) ? 1 : 0;
   p.err = d->err;
   p.slots = nullptr;
@@ -632,7 +646,9 @@ int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const ui
   const int rc = launch_gemm_any(bm, (flags & BD_GEMM_B_E4M3) == 0, maps, p, grid,
                                  (flags & BD_GEMM_OVERLAP_PREV) != 0,
                                  as_stream(stream));
-  if (rc != BD_OK || !use_ws) return rc;
+  if (rc != BD_OK) return rc;
+  if (p.fixup_kernel) return launch_fixup(bm, p, tiles, grid, as_stream(stream));
+  if (!use_ws) return rc;
   return bd_splitk_reduce(static_cast<const float*>(workspace), c, bias, b_tensor_scale, M, N,
                           split_k, out_dtype, epilogue, stream);
 }

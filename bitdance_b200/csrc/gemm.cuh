@@ -64,7 +64,10 @@ constexpr RingDepths ring_depths(int BM) {
   if (BM <= 16) return {4, 4, 6, 2};
   if (BM <= 32) return {4, 4, 3, 2};
   if (BM <= 64) return {4, 2, 6, 2};
-  return {4, 2, 4, 2};
+  // 128-row tiles: four B slots fit only with two weight and two token slots, which the
+  // transcode warps and the epilogue warps release as soon as they hold the stage's words in
+  // registers (kEarlyRelease)
+  return {2, 4, 2, 2};
 }
 
 template <int BM>
@@ -73,6 +76,10 @@ struct GemmCfg {
   static constexpr int SB = ring_depths(BM).sb;
   static constexpr int ST = ring_depths(BM).st;
   static constexpr int kGroups = ring_depths(BM).groups;  // transcode warp groups
+  // weight stages released after their loads (guarded by a dependent store), token slots by
+  // the epilogue warps after their copy into tensor memory; otherwise after the B rows are
+  // stored and by the MMA's commit
+  static constexpr bool kEarlyRelease = BM == 128;
   // token ring: BM rows x 128 B per slot (one E2M3 code per byte, 128B-swizzled so the copy
   // into tensor memory reads without bank conflicts), and the BM E8M0 words of each slot in a
   // separate small ring.
@@ -89,10 +96,12 @@ struct GemmCfg {
   static constexpr int oW = ST * kTRowBytes;
   static constexpr int oB = oW + SW * kWStage;
   static constexpr int oSf = oB + SB * kBStage;  // SB x 256 E8M0 words staged for tensor memory
-  // magnitude table, 16 copies interleaved (entry e of copy j at e*128 + j*8): copy j sits in
-  // bank pair j whatever the row, lane l reads copy l % 16, so the 8-byte lookups of a warp
-  // take the minimum two shared-memory wavefronts (two lanes per bank pair)
-  static constexpr int kPermCopies = 16;  // a table row is 128 bytes: class words index it
+  // magnitude table, kPermCopies copies interleaved (entry e of copy j at e * 8 * kPermCopies
+  // + j * 8), lane l reads copy l % kPermCopies. With 16 copies (decode tiles) copy j sits in
+  // bank pair j whatever the row, so the 8-byte lookups of a warp take the minimum two
+  // shared-memory wavefronts; 128-row tiles keep 8 copies (measured faster there).
+  static constexpr int kPermCopies = BM <= 64 ? 16 : 8;
+  static constexpr int kRowShift = BM <= 64 ? 7 : 6;  // log2 of a table row's byte stride
   static constexpr int oPerm = oSf + SB * 1024;
   static constexpr int oTs = oPerm + 64 * 8 * kPermCopies;  // token scale ring
   static constexpr int oCtl = oTs + ST * kTScaleSlot;
@@ -121,7 +130,7 @@ struct GemmCfg {
                 "TMA shared-memory destinations 128-byte aligned");
   static_assert(SW <= 4 && SB <= 4 && ST <= 8, "control block sizes");
   static_assert(SW % kGroups == 0 && SB % kGroups == 0, "slots owned by one group");
-  static_assert(8 * kPermCopies == 128, "table rows are 128 bytes apart (class-word shifts)");
+  static_assert(8 * kPermCopies == (1 << kRowShift), "class-word shifts match the row stride");
 };
 
 struct GemmCtl {
@@ -131,6 +140,7 @@ struct GemmCtl {
   uint32_t fin_job;  // 1: this CTA finishes the tile of its last segment
   uint32_t abort_flag;
   uint32_t bcast;
+  uint32_t sink;  // target of the never-taken dependent store of an early weight-stage release
   TranscodeTables tab;  // scale-byte classes (E4M3 sideband only)
 };
 
@@ -148,6 +158,7 @@ struct GemmParams {
   int out_dtype, epilogue;
   int vec_out;                  // 1: C is 16-byte aligned (vector stores)
   int weights_early;            // 1: B is not written by the grid this one may overlap
+  int fixup_kernel;             // 1: stream-K partials are summed by streamk_fixup_kernel
   uint32_t* err;
 };
 
@@ -370,6 +381,14 @@ __device__ __forceinline__ int last_segment(const Schedule& sch, int c, Seg& las
   return n;
 }
 
+// 16 or 32 consecutive accumulator columns of this warp's lane quarter into registers.
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
+  static_assert(N == 16 || N == 32, "16 or 32 columns");
+  if constexpr (N == 16) tmem_ld_x16(taddr, r);
+  else tmem_ld_x32(taddr, r);
+}
+
 __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
@@ -414,7 +433,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
     }
     for (int s = 0; s < Cfg::ST; ++s) {
       mbar_init(smem_u32(&ctl.tfull[s]), 1);
-      mbar_init(smem_u32(&ctl.tempty[s]), 1);
+      mbar_init(smem_u32(&ctl.tempty[s]), Cfg::kEarlyRelease ? Cfg::kEpiWarps : 1);
     }
     for (int s = 0; s < Cfg::SB; ++s) {
       mbar_init(smem_u32(&ctl.bready[s]), Cfg::kEpiWarps);
@@ -540,7 +559,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
                             (k == sg.k0 && kk == 0) ? 0u : 1u);
           }
           tc_commit(smem_u32(&ctl.bempty[b.slot]));
-          tc_commit(smem_u32(&ctl.tempty[t.slot]));
+          if constexpr (!Cfg::kEarlyRelease) tc_commit(smem_u32(&ctl.tempty[t.slot]));
           b.next();
           t.next();
         }
@@ -595,7 +614,21 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
             q[r][c] = ld_shared_v4((smem_u32(st) + code_sw[r]) ^ (c << 4));
           sc[r] = *reinterpret_cast<const uint2*>(st + scale_off[r]);
         }
-        // The weight stage is released only after the B rows computed from it are stored
+        if constexpr (Cfg::kEarlyRelease) {
+          // Release the weight stage now: a store that depends on every loaded word (never
+          // taken, but the loads must complete before it can issue) comes before the arrive,
+          // so no load of the stage is pending when its next TMA fill lands.
+          uint32_t dep = sc[0].x ^ sc[0].y;
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) dep ^= q[r][c].x ^ q[r][c].y ^ q[r][c].z ^ q[r][c].w;
+          if (dep == 0x9E3779B9u && lane == 31) *reinterpret_cast<volatile uint32_t*>(&ctl.sink) = dep;
+          asm volatile("" ::"r"(dep) : "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&ctl.wempty[ws]));
+        }
+        // Otherwise the weight stage is released only after the B rows computed from it are stored
         // (below), never straight after the loads: the stores depend on every loaded word, so
         // the stage cannot be refilled while a load of it is still outstanding. An arrive
         // right after the loads (a release that orders this thread's stores, not its loads)
@@ -615,8 +648,11 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
             const uint32_t f = blk < 2 ? (sc[r].x >> (16 * blk)) : (sc[r].y >> (16 * (blk - 2)));
             uint32_t off0, off1;  // byte offsets of the two 16-blocks' table rows
             if constexpr (kClassWords) {
-              // class word: both rows times 128 (the byte stride of a row in the 16-copy table)
-              const uint32_t off_small = (f << 7) & 0x1F80u, off_big = (f << 1) & 0x380u;
+              // class word: both rows times the table's row stride (bits 0..5: the smaller
+              // exponent's row, bits 6..8: the other's mantissa bits = its row)
+              constexpr int kS = Cfg::kRowShift;
+              const uint32_t off_small = (f << kS) & (0x3Fu << kS);
+              const uint32_t off_big = (f << (kS - 6)) & (0x7u << kS);
               const bool first_big = (f & 0x200u) != 0;
               off0 = first_big ? off_big : off_small;
               off1 = first_big ? off_small : off_big;
@@ -653,7 +689,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         fence_proxy_async_smem();  // the tensor core reads the B tile through the async proxy
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(smem_u32(&ctl.wempty[ws]));
+          if constexpr (!Cfg::kEarlyRelease) mbar_arrive(smem_u32(&ctl.wempty[ws]));
           mbar_arrive(smem_u32(&ctl.sfready[bs]));
         }
       }
@@ -661,7 +697,8 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
     // the fix-up of the tile of this CTA's last segment, when this CTA finishes it, is shared
     // with the epilogue warps (workers 128.. of 640)
     Seg lastseg;
-    if (p.split_k == 0 && last_segment(sch, cta, lastseg) > 0 && lastseg.slot >= 0 &&
+    if (p.split_k == 0 && !p.fixup_kernel && last_segment(sch, cta, lastseg) > 0 &&
+        lastseg.slot >= 0 &&
         !*abort_flag &&
         mbar_wait(smem_u32(&ctl.fin_bar), 0, p.err, kErrWaitAccum, abort_flag) &&
         ctl.fin_job != 0) {
@@ -676,7 +713,9 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
     const int quarter = warp & 3;
     const int ep_tid = tid - 64;  // 0..127
     const int mrow = quarter * 32 + lane;  // token row of the tile (accumulator lane)
-    constexpr int kEB = 32;                // accumulator columns per tensor-memory load
+    // accumulator columns per tensor-memory load: 32 for decode tiles (half the load round trips
+    // of a drain), 16 for 128-row tiles (measured faster there)
+    constexpr int kEB = BM <= 64 ? 32 : 16;
     grid_dep_wait();  // C, bias and the workspace belong to the previous grid until it ends
     const uint32_t taddr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
     Seg lastseg;
@@ -720,6 +759,13 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         const uint32_t* tok = reinterpret_cast<const uint32_t*>(
             smem + Cfg::oTs + t.slot * Cfg::kTScaleSlot);
         const uint32_t tokw = mrow < BM ? tok[mrow] : 0u;
+        if constexpr (Cfg::kEarlyRelease) {
+          // the token rows went to tensor memory from registers and the scale is in a
+          // register: the token slot can be refilled
+          asm volatile("" ::"r"(tokw) : "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&ctl.tempty[t.slot]));
+        }
         const uint32_t* sf_stage = reinterpret_cast<const uint32_t*>(smem + Cfg::oSf + b.slot * 1024);
         uint32_t wv[8];
 #pragma unroll
@@ -754,7 +800,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
           for (int c0 = 0; c0 < ncols; c0 += kEB) {
             uint32_t r[kEB];
             __syncwarp();
-            tmem_ld_x32(taddr + c0, r);
+            tmem_ld_cols<kEB>(taddr + c0, r);
             tmem_ld_wait();
             if (row_ok) {
               float4* dst = reinterpret_cast<float4*>(slot + mrow * kTileN + c0);
@@ -769,6 +815,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&ctl.acc_empty));
+        if (p.fixup_kernel) continue;  // summed after this grid by streamk_fixup_kernel
         __threadfence();
         const int first = sch.cta_of(sg.tile * p.nks);
         const int last = sch.cta_of((sg.tile + 1) * p.nks - 1);
@@ -800,7 +847,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         for (int c0 = 0; c0 < ncols; c0 += kEB) {
           uint32_t r[kEB];
           __syncwarp();
-          tmem_ld_x32(taddr + c0, r);
+          tmem_ld_cols<kEB>(taddr + c0, r);
           tmem_ld_wait();
           if (!row_ok) continue;  // the warp meets again at the next __syncwarp
           float acc[kEB];
@@ -852,6 +899,29 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tbase, Cfg::kTmemCols);
   }
+}
+
+// Stream-K fix-up as its own grid (tiles of 64 or 128 token rows): a split tile's partials
+// are 32-128 KB per contributor and a tile can have ten contributors, more than one SM reads
+// quickly from L2, so every split tile is summed by kFixupBlocks CTAs instead of by its last
+// contributor. Same sums in the same (CTA) order as the in-kernel fix-up, so the same bits.
+// Block b handles tile b / kFixupBlocks; tiles computed by one CTA were written by the GEMM.
+constexpr int kFixupBlocks = 16;
+constexpr int kFixupThreads = 256;
+
+template <int BM>
+__global__ void __launch_bounds__(kFixupThreads)
+    streamk_fixup_kernel(const GemmParams p, int gemm_grid) {
+  Schedule sch;
+  sch.init(p, gemm_grid);
+  Seg sg;
+  sg.tile = blockIdx.x / kFixupBlocks;
+  const int part = blockIdx.x % kFixupBlocks;
+  const int first = sch.cta_of(sg.tile * p.nks);
+  const int last = sch.cta_of((sg.tile + 1) * p.nks - 1);
+  if (first == last) return;
+  streamk_reduce<BM>(p, sch, sg, first, last, part * kFixupThreads + threadIdx.x,
+                     kFixupBlocks * kFixupThreads);
 }
 
 // Sum of fp32 partial planes -> C with scale, bias and activation. Vectorised by 4 along N.

@@ -180,6 +180,16 @@ __device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdes
   asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
                : "memory");
 }
+// Shared -> tensor memory: 128 rows (lanes) x 16 bytes (4 columns).
+__device__ __forceinline__ void tmem_cp_128x128b(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x128b [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
+// Shared -> tensor memory: 128 rows (lanes) x 32 bytes (8 columns).
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
 
 __device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(

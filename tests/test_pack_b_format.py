@@ -34,10 +34,10 @@ def pair_sideband(c0, c1):
 
 def decode_sideband(f):
     """GEMM: table rows (d*8 + mb) of the two 16-blocks and the E8M0 byte."""
-    off_small, off_big = (f << 7) & 0x1F80, (f << 1) & 0x380   # rows x 128 (16-copy table)
+    off_small, off_big = (f << 6) & 0xFC0, f & 0x1C0   # rows x 64 (8-copy table)
     first_big = (f & 0x200) != 0
-    row0 = np.where(first_big, off_big, off_small) // 128
-    row1 = np.where(first_big, off_small, off_big) // 128
+    row0 = np.where(first_big, off_big, off_small) // 64
+    row1 = np.where(first_big, off_small, off_big) // 64
     return row0, row1, ((f >> 10) & 0x1F) + 118
 
 
