@@ -29,11 +29,13 @@
 //   warp 1      MMA              4 block-scaled tcgen05.mma per chunk (A = tokens from tensor
 //                                memory, B = transcoded weights from shared memory); its
 //                                commits free the B and token slots.
-//   warps 2..5  epilogue         per chunk (one warp per tensor-memory lane quarter): the
-//                                quarter's token rows (the MMA's A operand) and the token and
-//                                weight scale factors into tensor memory (tcgen05.st); per
-//                                segment:
-//                                tensor-memory accumulator -> registers -> C / partials.
+//   warps 2..5  epilogue         one warp per tensor-memory lane quarter. Per chunk, for
+//                                128-row token tiles: the quarter's token rows (the MMA's A
+//                                operand) and the token and weight scale factors into tensor
+//                                memory (tcgen05.st); decode tiles (BM <= 64) have the
+//                                transcode group that converted the chunk do this itself
+//                                (kGroupDelivers). Per segment: tensor-memory accumulator ->
+//                                registers -> C / partials.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -72,6 +74,7 @@ constexpr RingDepths ring_depths(int BM) {
 
 template <int BM>
 struct GemmCfg {
+  static constexpr int kBM = BM;
   static constexpr int SW = ring_depths(BM).sw;
   static constexpr int SB = ring_depths(BM).sb;
   static constexpr int ST = ring_depths(BM).st;
@@ -80,6 +83,10 @@ struct GemmCfg {
   // the epilogue warps after their copy into tensor memory; otherwise after the B rows are
   // stored and by the MMA's commit
   static constexpr bool kEarlyRelease = BM == 128;
+  // decode tiles: the transcode group that converted a chunk also writes the chunk's token rows
+  // and scale factors into tensor memory and signals the MMA itself (one hand-off fewer per
+  // chunk); 128-row tiles leave that to the epilogue warps (measured faster there)
+  static constexpr bool kGroupDelivers = BM <= 64;
   // token ring: BM rows x 128 B per slot (one E2M3 code per byte, 128B-swizzled so the copy
   // into tensor memory reads without bank conflicts), and the BM E8M0 words of each slot in a
   // separate small ring.
@@ -405,6 +412,30 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                : "memory");
 }
 
+// Token row `mrow` of token slot `ts` (one E2M3 code per byte, 128B-swizzled as the TMA wrote
+// it) into the tensor-memory A slot at `dst` (this warp's lane quarter, lane = token row), the
+// codes' bits 6..7 cleared; rows >= BM are written as zeros. Executed by a whole warp.
+template <class Cfg>
+__device__ __forceinline__ void copy_token_rows(const uint8_t* smem, int ts, int mrow, uint32_t dst) {
+  uint32_t av[32];
+  if (mrow < Cfg::kBM) {
+    const uint8_t* trow =
+        smem + Cfg::oT + ts * Cfg::kTRowBytes + (mrow >> 3) * 1024 + (mrow & 7) * 128;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 v = *reinterpret_cast<const uint4*>(trow + ((c ^ (mrow & 7)) << 4));
+      av[4 * c + 0] = v.x & 0x3F3F3F3Fu;
+      av[4 * c + 1] = v.y & 0x3F3F3F3Fu;
+      av[4 * c + 2] = v.z & 0x3F3F3F3Fu;
+      av[4 * c + 3] = v.w & 0x3F3F3F3Fu;
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 32; ++c) av[c] = 0u;
+  }
+  tmem_st_x32(dst, av);
+}
+
 // kClassWords: B in bd_pack_b's transcode-ready layout (moved sign bits, class words); else
 // the E4M3 sideband (bd_pack_b_e4m3: the reference's codes and scale bytes, regrouped).
 template <int BM, bool kClassWords>
@@ -436,7 +467,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
       mbar_init(smem_u32(&ctl.tempty[s]), Cfg::kEarlyRelease ? Cfg::kEpiWarps : 1);
     }
     for (int s = 0; s < Cfg::SB; ++s) {
-      mbar_init(smem_u32(&ctl.bready[s]), Cfg::kEpiWarps);
+      mbar_init(smem_u32(&ctl.bready[s]), Cfg::kGroupDelivers ? Cfg::kGroupWarps : Cfg::kEpiWarps);
       mbar_init(smem_u32(&ctl.bempty[s]), 1);
       mbar_init(smem_u32(&ctl.sfready[s]), Cfg::kGroupWarps);
     }
@@ -692,6 +723,43 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
           if constexpr (!Cfg::kEarlyRelease) mbar_arrive(smem_u32(&ctl.wempty[ws]));
           mbar_arrive(smem_u32(&ctl.sfready[bs]));
         }
+        if constexpr (Cfg::kGroupDelivers) {
+          // The chunk's operands into tensor memory, by this group: warps 0..3 of the group (one
+          // per lane quarter) the quarter's token rows and token scales; warps 4..7 the weight
+          // scales, once every warp of the group has staged its rows' words (sfready; a bounded
+          // wait, so a warp that gave up earlier makes this one time out, not hang). The MMA
+          // waits for all eight warps (bready).
+          const int quarter = warp & 3;
+          const int mrow = quarter * 32 + lane;
+          const uint32_t taddr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
+          const uint32_t col = taddr + Cfg::kSfCol0 + bs * Cfg::kSfCols;
+          const int ts = ci % Cfg::ST;
+          bool ok = true;
+          if ((tw % Cfg::kGroupWarps) < 4) {
+            ok = mbar_wait(smem_u32(&ctl.tfull[ts]), (ci / Cfg::ST) & 1, p.err, kErrWaitTma,
+                           abort_flag);
+            if (ok) {
+              if (quarter * 32 < BM) copy_token_rows<Cfg>(smem, ts, mrow, taddr + Cfg::kACol0 + bs * 32);
+              const uint32_t* tok =
+                  reinterpret_cast<const uint32_t*>(smem + Cfg::oTs + ts * Cfg::kTScaleSlot);
+              tmem_st_x1(col + quarter, mrow < BM ? tok[mrow] : 0u);
+            }
+          } else {
+            ok = mbar_wait(smem_u32(&ctl.sfready[bs]), (ci / Cfg::SB) & 1, p.err,
+                           kErrWaitOperand, abort_flag);
+            if (ok) {
+              uint32_t wv[8];
+#pragma unroll
+              for (int c = 0; c < 8; ++c) wv[c] = sf_stage[32 * c + lane];
+              tmem_st_x8(col + 4, wv);
+            }
+          }
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (!ok) break;
+          if (lane == 0) mbar_arrive(smem_u32(&ctl.bready[bs]));
+        }
       }
     }
     // the fix-up of the tile of this CTA's last segment, when this CTA finishes it, is shared
@@ -729,33 +797,14 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
       // column 4 + c (every quarter holds a copy of the weight scales). Staged by the
       // transcode warps (sfready); the MMA waits for all four quarters (bready).
       bool ok = true;
-      for (int k = sg.k0; k < sg.k1; ++k) {
+      for (int k = sg.k0; k < sg.k1 && !Cfg::kGroupDelivers; ++k) {
         if (!mbar_wait(smem_u32(&ctl.sfready[b.slot]), b.phase, p.err, kErrWaitOperand,
                        abort_flag) ||
             !mbar_wait(smem_u32(&ctl.tfull[t.slot]), t.phase, p.err, kErrWaitTma, abort_flag)) {
           ok = false;
           break;
         }
-        if (quarter * 32 < BM) {
-          // token rows of this lane quarter -> tensor-memory A slot (lane m = token m)
-          uint32_t av[32];
-          if (mrow < BM) {
-            const uint8_t* trow = smem + Cfg::oT + t.slot * Cfg::kTRowBytes + (mrow >> 3) * 1024 +
-                                  (mrow & 7) * 128;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              const uint4 v = *reinterpret_cast<const uint4*>(trow + ((c ^ (mrow & 7)) << 4));
-              av[4 * c + 0] = v.x & 0x3F3F3F3Fu;
-              av[4 * c + 1] = v.y & 0x3F3F3F3Fu;
-              av[4 * c + 2] = v.z & 0x3F3F3F3Fu;
-              av[4 * c + 3] = v.w & 0x3F3F3F3Fu;
-            }
-          } else {
-#pragma unroll
-            for (int c = 0; c < 32; ++c) av[c] = 0u;
-          }
-          tmem_st_x32(taddr + Cfg::kACol0 + b.slot * 32, av);
-        }
+        if (quarter * 32 < BM) copy_token_rows<Cfg>(smem, t.slot, mrow, taddr + Cfg::kACol0 + b.slot * 32);
         const uint32_t* tok = reinterpret_cast<const uint32_t*>(
             smem + Cfg::oTs + t.slot * Cfg::kTScaleSlot);
         const uint32_t tokw = mrow < BM ? tok[mrow] : 0u;
