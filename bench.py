@@ -168,12 +168,24 @@ def blas_threads():
     return None
 
 
-def cpu_reference_run(seconds=10.0, rows=512):
-    """Per GEMM of the decode sweep: NVFP4 -> MXFP6 transcode of a `rows`-row slice of the
-    weights (C restatement, all host threads), then the GEMM: dequantisation and an fp32 matmul
-    (OpenBLAS) with M tokens; the two parts are timed separately. Returns a dict with the
-    weight GB/s of the whole path and of each part, the seconds per GEMM of each part (scaled
-    to the full 14336-row matrix), the thread counts and the sample description."""
+def all_blas_threads(cores):
+    """OpenBLAS limited to `cores` threads for the duration of a with block (torchrun sets
+    OMP_NUM_THREADS=1 for its workers; the CPU path gets every host core)."""
+    try:
+        from threadpoolctl import threadpool_limits
+        return threadpool_limits(limits=cores, user_api="blas")
+    except Exception:  # noqa: BLE001 - no threadpoolctl: the library default applies
+        import contextlib
+        return contextlib.nullcontext()
+
+
+def cpu_reference_run(seconds=10.0, rows=N_W):
+    """The decode sweep on the CPU: per GEMM, the NVFP4 -> MXFP6 transcode of the whole
+    `rows` x 4096 weight matrix (C restatement, all host threads), then the GEMM: dequantisation
+    and an fp32 matmul (OpenBLAS, all host threads) with M tokens; the two parts are timed
+    separately, whole sweeps (M = 1, 4, 16, 32, 64) until `seconds` have passed. Returns a dict
+    with the weight GB/s of the whole path and of each part, the seconds per GEMM of each part,
+    the thread counts and the sample description."""
     import numpy as np
     lib = _orc()
     cores = os.cpu_count() or 1
@@ -188,35 +200,36 @@ def cpu_reference_run(seconds=10.0, rows=512):
     acts = {M: rng.standard_normal((M, K)).astype(np.float32) for M in M_SWEEP}
     done = 0
     t_tx = t_mm = 0.0
-    t0 = time.perf_counter()
-    while True:
-        for M in M_SWEEP:
-            a = time.perf_counter()
-            lib.orc_transcode(packed.ctypes.data, scales.ctypes.data, nblk, 16, e6.ctypes.data,
-                              e8.ctypes.data, cores)
-            b = time.perf_counter()
-            lib.orc_dequant(e6.ctypes.data, e8.ctypes.data, nblk, Bf.ctypes.data, cores)
-            _ = acts[M] @ Bf.T
-            c = time.perf_counter()
-            t_tx += b - a
-            t_mm += c - b
-            done += 1
-        el = time.perf_counter() - t0
-        if el >= seconds:
-            break
+    with all_blas_threads(cores):
+        blas = blas_threads()
+        t0 = time.perf_counter()
+        while True:
+            for M in M_SWEEP:
+                a = time.perf_counter()
+                lib.orc_transcode(packed.ctypes.data, scales.ctypes.data, nblk, 16,
+                                  e6.ctypes.data, e8.ctypes.data, cores)
+                b = time.perf_counter()
+                lib.orc_dequant(e6.ctypes.data, e8.ctypes.data, nblk, Bf.ctypes.data, cores)
+                _ = acts[M] @ Bf.T
+                c = time.perf_counter()
+                t_tx += b - a
+                t_mm += c - b
+                done += 1
+            el = time.perf_counter() - t0
+            if el >= seconds:
+                break
     wb = weight_bytes(rows, K)
-    scale_full = N_W / rows
     return {
         "value": done * wb / (t_tx + t_mm) / 1e9,
         "transcode_gbs": done * wb / t_tx / 1e9,
         "gemm_gbs": done * wb / t_mm / 1e9,
-        "transcode_s_per_gemm": t_tx / done * scale_full,
-        "gemm_s_per_gemm": t_mm / done * scale_full,
+        "transcode_s_per_gemm": t_tx / done,
+        "gemm_s_per_gemm": t_mm / done,
         "cores": cores,
-        "blas": blas_threads(),
-        "sample": (f"{done} GEMMs of the M sweep on a {rows}x{K} weight slice "
-                   f"(transcode {t_tx:.1f} s + dequant and fp32 matmul {t_mm:.1f} s), "
-                   f"{el:.1f} s; per-GEMM seconds scaled to N={N_W}"),
+        "blas": blas,
+        "sample": (f"{done // len(M_SWEEP)} decode sweeps ({done} GEMMs) on the whole {rows}x{K} "
+                   f"weight matrix (transcode {t_tx:.1f} s + dequant and fp32 matmul "
+                   f"{t_mm:.1f} s), {el:.1f} s"),
     }
 
 
@@ -239,6 +252,8 @@ def cpu_config_rates(seconds=4.0):
     A = rng.standard_normal((M, K)).astype(np.float32)
     t_tx = t_mm = 0.0
     n = 0
+    limits = all_blas_threads(cores)
+    limits.__enter__()
     t0 = time.perf_counter()
     while time.perf_counter() - t0 < seconds:
         a = time.perf_counter()
@@ -251,6 +266,7 @@ def cpu_config_rates(seconds=4.0):
         t_tx += b - a
         t_mm += c - b
         n += 1
+    limits.__exit__(None, None, None)
     return {"transcode_bytes_per_s": n * weight_bytes(rows, K) / t_tx,
             "gemm_flops_per_s": n * 2.0 * M * rows * K / t_mm,
             "dequant_matmul_shape": f"M={M} x {rows}x{K}", "iterations": n}
