@@ -189,7 +189,7 @@ StreamKSizes streamk_sizes(int M, int N, int K, int sm_count) {
 }
 
 struct GemmMaps {
-  CUtensorMap a, as, w, ws;
+  CUtensorMap a, as, w, ws, c;  // c: 16-bit C for TMA stores (GemmParams::tma_c), else zeros
 };
 
 template <int BM, bool kClassWords>
@@ -217,7 +217,7 @@ int launch_gemm(const GemmMaps& m, const GemmParams& p, int grid, bool overlap,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = overlap ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, w4a6_gemm_kernel<BM, kClassWords>, m.a, m.as, m.w, m.ws, p) !=
+  if (cudaLaunchKernelEx(&cfg, w4a6_gemm_kernel<BM, kClassWords>, m.a, m.as, m.w, m.ws, m.c, p) !=
       cudaSuccess)
     return BD_ERR_CUDA;
   return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
@@ -627,6 +627,17 @@ int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const ui
   // own (many SMs) instead of by each tile's last contributor (one SM)
   p.fixup_kernel = (streamk && bm >= 64) ? 1 : 0;
   p.vec_out = aligned(c, 16) ? 1 : 0;
+  // whole 128-row tiles of a 16-bit C store through shared memory with TMA: boxes of 32 rows x
+  // 32 outputs (64 B, the 64B swizzle span); the row pitch 2N is a multiple of 256 B
+  std::memset(&maps.c, 0, sizeof(maps.c));
+  p.tma_c = 0;
+  if (bm == 128 && split_mode != BD_SPLIT_ATOMIC && split_k <= 1 && out_dtype != BD_OUT_F32 &&
+      p.vec_out) {
+    if (!make_map_2d(&maps.c, CU_TENSOR_MAP_DATA_TYPE_UINT16, c, N, M,
+                     static_cast<uint64_t>(N) * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+      return BD_ERR_CUDA;
+    p.tma_c = 1;
+  }
   p.err = d->err;
   p.slots = nullptr;
   p.counters = nullptr;

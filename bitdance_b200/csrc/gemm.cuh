@@ -111,7 +111,12 @@ struct GemmCfg {
   static constexpr int kRowShift = BM <= 64 ? 7 : 6;  // log2 of a table row's byte stride
   static constexpr int oPerm = oSf + SB * 1024;
   static constexpr int oTs = oPerm + 64 * 8 * kPermCopies;  // token scale ring
-  static constexpr int oCtl = oTs + ST * kTScaleSlot;
+  // 128-row tiles write C through shared memory with TMA stores (GemmParams::tma_c): per
+  // epilogue warp two 2 KB staging buffers of 32 rows x 64 B (32 16-bit outputs), 64B-swizzled
+  static constexpr bool kTmaStore = BM == 128;
+  static constexpr int kCStage = 2048;
+  static constexpr int oC = kTmaStore ? cround(oTs + ST * kTScaleSlot, 1024) : oTs + ST * kTScaleSlot;
+  static constexpr int oCtl = oC + (kTmaStore ? 4 * 2 * kCStage : 0);
   static constexpr int kCtlBytes = 1024;
   static constexpr int kSmemBytes = oCtl + kCtlBytes + 1024;  // + alignment slack
   // tensor memory: accumulator (256 columns) | per B slot the A operand (token m at lane m,
@@ -135,6 +140,7 @@ struct GemmCfg {
   static_assert(oW % 1024 == 0 && oB % 1024 == 0 && kTRowBytes % 1024 == 0, "1 KB swizzle atoms");
   static_assert(oTs % 128 == 0 && kTScaleSlot % 128 == 0 && kWCodes % 128 == 0,
                 "TMA shared-memory destinations 128-byte aligned");
+  static_assert(!kTmaStore || oC % 1024 == 0, "64B-swizzled staging buffers 1 KB aligned");
   static_assert(SW <= 4 && SB <= 4 && ST <= 8, "control block sizes");
   static_assert(SW % kGroups == 0 && SB % kGroups == 0, "slots owned by one group");
   static_assert(8 * kPermCopies == (1 << kRowShift), "class-word shifts match the row stride");
@@ -166,6 +172,7 @@ struct GemmParams {
   int vec_out;                  // 1: C is 16-byte aligned (vector stores)
   int weights_early;            // 1: B is not written by the grid this one may overlap
   int fixup_kernel;             // 1: stream-K partials are summed by streamk_fixup_kernel
+  int tma_c;                    // 1: whole 128-row tiles store C (16-bit) with TMA (tm_c)
   uint32_t* err;
 };
 
@@ -231,6 +238,32 @@ __device__ __forceinline__ float apply_epilogue(float v, int epi, const __nv_bfl
     v = 0.5f * v * (1.0f + tanhf(y));
   }
   return v;
+}
+
+// The same for NV consecutive outputs n .. n + NV - 1, scaled first: the epilogue kind is
+// tested once per row piece, not per element (a per-element test in an unrolled drain loop
+// cost more than the conversion itself), with the same operations in the same order.
+template <int NV>
+__device__ __forceinline__ void apply_epilogue_row(float (&v)[NV], float scale, int epi,
+                                                   const __nv_bfloat16* bias, int n) {
+#pragma unroll
+  for (int j = 0; j < NV; ++j) v[j] *= scale;
+  if (epi == 0) return;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) v[j] += __bfloat162float(bias[n + j]);
+  if (epi == 2) {
+#pragma unroll
+    for (int j = 0; j < NV; ++j) v[j] = fmaxf(v[j], 0.0f);
+  } else if (epi == 3) {
+#pragma unroll
+    for (int j = 0; j < NV; ++j) v[j] = v[j] / (1.0f + expf(-v[j]));
+  } else if (epi == 4) {
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const float y = 0.7978845608028654f * (v[j] + 0.044715f * v[j] * v[j] * v[j]);
+      v[j] = 0.5f * v[j] * (1.0f + tanhf(y));
+    }
+  }
 }
 
 __device__ __forceinline__ void store_out(void* out, int64_t idx, float v, int dtype) {
@@ -369,9 +402,7 @@ __device__ __forceinline__ void streamk_reduce(const GemmParams& p, const Schedu
       if (gi >= total) break;
       const int rr = off[u] / kTileN, n = n0 + (off[u] - rr * kTileN);
       float o[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        o[j] = apply_epilogue(o[j] * p.tensor_scale, p.epilogue, p.bias, n + j);
+      apply_epilogue_row<4>(o, p.tensor_scale, p.epilogue, p.bias, n);
       store_row<4>(p.out, static_cast<int64_t>(m0 + rr) * p.N + n, o, p.out_dtype, p.vec_out);
     }
   }
@@ -443,7 +474,8 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
     w4a6_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
                      const __grid_constant__ CUtensorMap tm_as,
                      const __grid_constant__ CUtensorMap tm_w,
-                     const __grid_constant__ CUtensorMap tm_ws, const GemmParams p) {
+                     const __grid_constant__ CUtensorMap tm_ws,
+                     const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
   using Cfg = GemmCfg<BM>;
   static_assert(sizeof(GemmCtl) <= Cfg::kCtlBytes, "control block");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -788,6 +820,9 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
     const uint32_t taddr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
     Seg lastseg;
     const int nseg = last_segment(sch, cta, lastseg);
+    // this warp's C staging buffers and the count of its TMA stores (kTmaStore)
+    const uint32_t cstage = smem_u32(smem + Cfg::oC) + quarter * 2 * Cfg::kCStage;
+    int c_stores = 0;
     RingPos<Cfg::SB> b;
     RingPos<Cfg::ST> t;
     Seg sg;
@@ -892,6 +927,60 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         }
         continue;
       }
+      if constexpr (Cfg::kTmaStore) {
+        if (p.tma_c) {
+          // 32 columns at a time: converted to 16-bit, staged (row = lane, 64B-swizzled) and
+          // stored by one TMA store per warp, which clips rows >= M; a staging buffer is
+          // rewritten once the store issued two steps earlier has read it
+          if (warp_rows) {
+            for (int c0 = 0; c0 < ncols; c0 += 32) {
+              uint32_t r[32];
+              __syncwarp();
+              tmem_ld_x32(taddr + c0, r);
+              tmem_ld_wait();
+              const int n = n0 + c0;
+              float f[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+              apply_epilogue_row<32>(f, p.tensor_scale, p.epilogue, p.bias, n);
+              uint32_t wv[16];
+              if (p.out_dtype == 0) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const __nv_bfloat162 b2 = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+                  wv[j] = *reinterpret_cast<const uint32_t*>(&b2);
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const __half2 h2 = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+                  wv[j] = *reinterpret_cast<const uint32_t*>(&h2);
+                }
+              }
+              const uint32_t sb = cstage + (c_stores & 1) * Cfg::kCStage;
+              if (c_stores >= 2) {
+                if (lane == 0) bulk_wait_group_read<1>();
+                __syncwarp();
+              }
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                st_shared_v4(sb + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4), wv[4 * q],
+                             wv[4 * q + 1], wv[4 * q + 2], wv[4 * q + 3]);
+              fence_proxy_async_smem();  // the TMA store reads the staging through the async proxy
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&tm_c, sb, n, m0 + quarter * 32);
+                bulk_commit_group();
+              }
+              ++c_stores;
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&ctl.acc_empty));
+          continue;
+        }
+      }
       if (warp_rows) {
         for (int c0 = 0; c0 < ncols; c0 += kEB) {
           uint32_t r[kEB];
@@ -909,9 +998,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
 #pragma unroll
             for (int j = 0; j < kEB; ++j) atomicAdd(o + j, acc[j] * p.tensor_scale);
           } else if (p.split_k <= 1) {
-#pragma unroll
-            for (int j = 0; j < kEB; ++j)
-              acc[j] = apply_epilogue(acc[j] * p.tensor_scale, p.epilogue, p.bias, n + j);
+            apply_epilogue_row<kEB>(acc, p.tensor_scale, p.epilogue, p.bias, n);
             store_row<kEB>(p.out, rowbase, acc, p.out_dtype, p.vec_out);
           } else if (p.split_out == kOutPartial) {
             float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) +
@@ -935,6 +1022,8 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&ctl.acc_empty));
     }
+    // this warp's TMA stores of C complete before the grid does
+    if (Cfg::kTmaStore && c_stores > 0 && lane == 0) bulk_wait_group_all();
   }
 
   // ------------------------------------------------------------------ teardown

@@ -357,3 +357,38 @@ def test_both_weight_layouts_give_the_same_bytes(M, N, K, split_k):
     assert torch.equal(out[0], out[1])
     C, Cabs = gold(*ops, 0.5)
     check(out[0], C, Cabs, torch.float32)
+
+
+@pytest.mark.parametrize("M,out_dtype,epi", [(200, torch.float16, "bias_gelu"),
+                                             (300, torch.bfloat16, "bias_relu"),
+                                             (129, torch.float16, "none")])
+def test_token_tiles_of_128_rows_store_paths(M, out_dtype, epi):
+    """128-row token tiles write C with TMA stores from shared memory: 16-bit outputs with an
+    epilogue, rows past M left untouched (C is a view into a larger buffer with guard rows),
+    and the same values through the per-thread store path when C is not 16-byte aligned."""
+    import bitdance_b200 as bd
+    N, K = 512, 512
+    ops = random_operands(M, N, K, seed=M + 5, b_scale_lo=0x18, b_scale_hi=0x30)
+    bias = (np.random.default_rng(M).standard_normal(N) * 2).astype(np.float32)
+    bias_bf = torch.from_numpy(bias).to(torch.bfloat16)
+    C, Cabs = gold(*ops, 0.05, bias_bf.float().numpy().astype(np.float64) if epi != "none" else None)
+    if epi == "bias_relu":
+        C = np.maximum(C, 0)
+    elif epi == "bias_gelu":
+        C = 0.5 * C * (1 + np.tanh(0.7978845608028654 * (C + 0.044715 * C ** 3)))
+    acts = bd.pack_activations(dev(ops[0]), dev(ops[1]))
+    w = bd.pack_weights(dev(ops[2]), dev(ops[3]), 0.05)
+    kw = dict(out_dtype=out_dtype, split_k=1, epilogue=epi,
+              bias=bias_bf.cuda() if epi != "none" else None)
+    big = torch.full((M + 8, N), float("nan"), dtype=out_dtype, device="cuda")
+    got = bd.w4a6_gemm(acts, w, out=big[:M], **kw)
+    # the same GEMM into a C that starts 2 bytes past a 16-byte boundary
+    flat = torch.full((M * N + 8,), float("nan"), dtype=out_dtype, device="cuda")
+    odd = bd.w4a6_gemm(acts, w, out=flat[1:1 + M * N].view(M, N), **kw)
+    torch.cuda.synchronize()
+    assert bd.device_error() == 0
+    assert bool(torch.isnan(big[M:]).all()), "rows past M were written"
+    assert bool(torch.isnan(flat[0])) and bool(torch.isnan(flat[1 + M * N:]).all())
+    g = got.float().cpu().numpy().astype(np.float64)
+    assert o.rel_linf(C, g) <= TOL_REL_LINF
+    assert torch.equal(got, odd)
