@@ -59,12 +59,18 @@ constexpr int kTileN = 256;  // weight rows per tile (the MMA's N)
 // transcode warps), B ring SB (transcoded operand, released by the MMA), token ring ST, and G,
 // the number of transcode warp groups that take chunks in turn. SW and SB are multiples of G,
 // so a slot is only ever used by one group, in order: no waiter can run a whole phase ahead.
+// When the groups also take the token slots (kGroupDelivers), ST is a multiple of G for the
+// same reason: a group waiting on a token slot has itself consumed the slot's previous fill, so
+// the fill it waits for is never two phases ahead of the barrier (a parity wait would pass on
+// the older phase and copy stale token rows). Decode tiles of up to 32 rows use four groups of
+// four warps (two weight rows per thread): four chunks in flight, measured 2 % faster than
+// two groups of eight there.
 struct RingDepths {
   int sw, sb, st, groups;
 };
 constexpr RingDepths ring_depths(int BM) {
-  if (BM <= 16) return {4, 4, 6, 2};
-  if (BM <= 32) return {4, 4, 3, 2};
+  if (BM <= 16) return {4, 4, 4, 4};
+  if (BM <= 32) return {4, 4, 4, 4};
   if (BM <= 64) return {4, 2, 6, 2};
   // 128-row tiles: four B slots fit only with two weight and two token slots, which the
   // transcode warps and the epilogue warps release as soon as they hold the stage's words in
@@ -106,9 +112,10 @@ struct GemmCfg {
   // magnitude table, kPermCopies copies interleaved (entry e of copy j at e * 8 * kPermCopies
   // + j * 8), lane l reads copy l % kPermCopies. With 16 copies (decode tiles) copy j sits in
   // bank pair j whatever the row, so the 8-byte lookups of a warp take the minimum two
-  // shared-memory wavefronts; 128-row tiles keep 8 copies (measured faster there).
-  static constexpr int kPermCopies = BM <= 64 ? 16 : 8;
-  static constexpr int kRowShift = BM <= 64 ? 7 : 6;  // log2 of a table row's byte stride
+  // shared-memory wavefronts; 128-row tiles keep 8 copies (measured faster there), and so do
+  // 32-row tiles, whose four token slots leave no room for 16.
+  static constexpr int kPermCopies = (BM <= 64 && BM != 32) ? 16 : 8;
+  static constexpr int kRowShift = (BM <= 64 && BM != 32) ? 7 : 6;  // log2 of a table row's stride
   static constexpr int oPerm = oSf + SB * 1024;
   static constexpr int oTs = oPerm + 64 * 8 * kPermCopies;  // token scale ring
   // 128-row tiles write C through shared memory with TMA stores (GemmParams::tma_c): per
@@ -130,6 +137,7 @@ struct GemmCfg {
   static constexpr int kTmemCols = 512;
   static constexpr int kTranscodeWarps = 16;
   static constexpr int kGroupWarps = kTranscodeWarps / kGroups;
+  static_assert(kGroupWarps == 4 || kGroupWarps == 8, "delivery roles need four or eight warps");
   static constexpr int kRowsPerThread = 256 / (32 * kGroupWarps);
   static constexpr int kEpiWarps = 4;
   static constexpr int kTProducerWarp = 2 + kEpiWarps + kTranscodeWarps;  // 22
@@ -143,6 +151,7 @@ struct GemmCfg {
   static_assert(!kTmaStore || oC % 1024 == 0, "64B-swizzled staging buffers 1 KB aligned");
   static_assert(SW <= 4 && SB <= 4 && ST <= 8, "control block sizes");
   static_assert(SW % kGroups == 0 && SB % kGroups == 0, "slots owned by one group");
+  static_assert(!kGroupDelivers || ST % kGroups == 0, "token slots owned by one group");
   static_assert(8 * kPermCopies == (1 << kRowShift), "class-word shifts match the row stride");
 };
 
@@ -757,17 +766,20 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         }
         if constexpr (Cfg::kGroupDelivers) {
           // The chunk's operands into tensor memory, by this group: warps 0..3 of the group (one
-          // per lane quarter) the quarter's token rows and token scales; warps 4..7 the weight
-          // scales, once every warp of the group has staged its rows' words (sfready; a bounded
-          // wait, so a warp that gave up earlier makes this one time out, not hang). The MMA
-          // waits for all eight warps (bready).
+          // per lane quarter) the quarter's token rows and token scales; the weight scales, once
+          // every warp of the group has staged its rows' words (sfready; a bounded wait, so a
+          // warp that gave up earlier makes this one time out, not hang), by warps 4..7 of an
+          // eight-warp group and by every warp of a four-warp group. The MMA waits for all the
+          // group's warps (bready).
           const int quarter = warp & 3;
           const int mrow = quarter * 32 + lane;
           const uint32_t taddr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
           const uint32_t col = taddr + Cfg::kSfCol0 + bs * Cfg::kSfCols;
           const int ts = ci % Cfg::ST;
+          const int gw = tw % Cfg::kGroupWarps;
+          const bool sf_role = Cfg::kGroupWarps == 4 || gw >= 4;
           bool ok = true;
-          if ((tw % Cfg::kGroupWarps) < 4) {
+          if (gw < 4) {
             ok = mbar_wait(smem_u32(&ctl.tfull[ts]), (ci / Cfg::ST) & 1, p.err, kErrWaitTma,
                            abort_flag);
             if (ok) {
@@ -776,7 +788,8 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
                   reinterpret_cast<const uint32_t*>(smem + Cfg::oTs + ts * Cfg::kTScaleSlot);
               tmem_st_x1(col + quarter, mrow < BM ? tok[mrow] : 0u);
             }
-          } else {
+          }
+          if (ok && sf_role) {
             ok = mbar_wait(smem_u32(&ctl.sfready[bs]), (ci / Cfg::SB) & 1, p.err,
                            kErrWaitOperand, abort_flag);
             if (ok) {
