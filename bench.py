@@ -389,7 +389,8 @@ def time_gemm_config(torch, ops, dev, M, N, K, w_kind, w_std, a_kind, seed, stre
     """One BASELINE config on one GPU: weights quantised on the GPU from the config's
     distribution, rotated over enough copies that the working set exceeds L2, the GEMMs of one
     pass captured in a CUDA graph (back to back, programmatic serialisation with static
-    weights). Returns ms per GEMM."""
+    weights), replayed for about 20 ms per timing; the median of three timings. Returns ms per
+    GEMM."""
     g = generator(torch, dev, seed)
     w = (gen_student_t(torch, (N, K), w_std, g) if w_kind == "t"
          else torch.randn((N, K), device=dev, generator=g) * w_std)
@@ -410,7 +411,9 @@ def time_gemm_config(torch, ops, dev, M, N, K, w_kind, w_std, a_kind, seed, stre
             ops.w4a6_gemm(acts, ws[i % reps], out=out, workspace=wsp, stream=stream,
                           overlap_prev=True, weights_static=True)
     graph = graph_of(torch, body, stream)
-    ms = time_graph(torch, graph, stream, iters=3) / n
+    per_replay = time_graph(torch, graph, stream, iters=1)
+    iters = max(3, int(20.0 / max(per_replay, 1e-3)))
+    ms = sorted(time_graph(torch, graph, stream, iters=iters, warmup=1) for _ in range(3))[1] / n
     del graph
     return ms
 

@@ -667,7 +667,20 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
       // likewise bits 4..6: chunk cc of row n at (slot + row offset + ((n & 7) << 4)) ^ (cc << 4)
       b_sw[r] = (row >> 3) * 1024 + (row & 7) * 128 + ((row & 7) << 4);
     }
-    const uint8_t* perm = smem + Cfg::oPerm + (lane % Cfg::kPermCopies) * 8;
+    // The stage bases are 1 KB aligned and the swizzles touch address bits 4..6 only, so
+    // (base + offset) ^ (c << 4) == base + (offset ^ (c << 4)): the swizzled offsets of this
+    // thread's first row are computed once, a further row of the thread is a fixed distance
+    // on (rows 128 apart), and every access is a warp-uniform base plus a per-thread offset.
+    static_assert(R == 1 || 32 * Cfg::kGroupWarps == 128, "further rows 128 rows on");
+    constexpr int kCodeRowStep = 8192, kScaleRowStep = 1024, kBRowStep = 16384;
+    uint32_t code_off[4], b_off[8];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) code_off[c] = static_cast<uint32_t>(code_sw[0]) ^ (c << 4);
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc) b_off[cc] = static_cast<uint32_t>(b_sw[0]) ^ (cc << 4);
+    // magnitude table: this lane's copy, as an offset OR-ed into each row's offset
+    const uint8_t* tab_p = smem + Cfg::oPerm;
+    const uint32_t lane_copy = (lane % Cfg::kPermCopies) * 8;
     int ci = 0;  // chunk number within this CTA
     Seg sg;
     for (int idx = 0; sch.segment(cta, idx, sg) && !*abort_flag; ++idx) {
@@ -679,22 +692,25 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         const uint8_t* st = smem + Cfg::oW + ws * Cfg::kWStage;
         uint4 q[R][4];
         uint2 sc[R];
+        const uint32_t st_u = smem_u32(st);
 #pragma unroll
         for (int r = 0; r < R; ++r) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            q[r][c] = ld_shared_v4((smem_u32(st) + code_sw[r]) ^ (c << 4));
-          sc[r] = *reinterpret_cast<const uint2*>(st + scale_off[r]);
+          for (int c = 0; c < 4; ++c) q[r][c] = ld_shared_v4(st_u + code_off[c] + r * kCodeRowStep);
+          sc[r] = *reinterpret_cast<const uint2*>(st + scale_off[0] + r * kScaleRowStep);
         }
         if constexpr (Cfg::kEarlyRelease) {
-          // Release the weight stage now: a store that depends on every loaded word (never
-          // taken, but the loads must complete before it can issue) comes before the arrive,
-          // so no load of the stage is pending when its next TMA fill lands.
-          uint32_t dep = sc[0].x ^ sc[0].y;
+          // Release the weight stage now: a store that depends on every load (never taken, but
+          // the loads must complete before it can issue; one word of a vector load completes
+          // with the others) comes before the arrive, so no load of the stage is pending when
+          // its next TMA fill lands.
+          uint32_t dep = 0;
 #pragma unroll
-          for (int r = 0; r < R; ++r)
+          for (int r = 0; r < R; ++r) {
+            dep ^= sc[r].x;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) dep ^= q[r][c].x ^ q[r][c].y ^ q[r][c].z ^ q[r][c].w;
+            for (int c = 0; c < 4; ++c) dep ^= q[r][c].x;
+          }
           if (dep == 0x9E3779B9u && lane == 31) *reinterpret_cast<volatile uint32_t*>(&ctl.sink) = dep;
           asm volatile("" ::"r"(dep) : "memory");
           __syncwarp();
@@ -723,20 +739,20 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
               // class word: both rows times the table's row stride (bits 0..5: the smaller
               // exponent's row, bits 6..8: the other's mantissa bits = its row)
               constexpr int kS = Cfg::kRowShift;
-              const uint32_t off_small = (f << kS) & (0x3Fu << kS);
-              const uint32_t off_big = (f << (kS - 6)) & (0x7u << kS);
+              const uint32_t off_small = ((f << kS) & (0x3Fu << kS)) | lane_copy;
+              const uint32_t off_big = ((f << (kS - 6)) & (0x7u << kS)) | lane_copy;
               const bool first_big = (f & 0x200u) != 0;
               off0 = first_big ? off_big : off_small;
               off1 = first_big ? off_small : off_big;
             } else {
               uint32_t i0, i1, e8;
               pair_class(ctl.tab, f & 0xFFu, (f >> 8) & 0xFFu, i0, i1, e8);
-              off0 = i0 * (8 * Cfg::kPermCopies);
-              off1 = i1 * (8 * Cfg::kPermCopies);
+              off0 = (i0 * (8 * Cfg::kPermCopies)) | lane_copy;
+              off1 = (i1 * (8 * Cfg::kPermCopies)) | lane_copy;
               sfw |= e8 << (8 * blk);
             }
-            const uint2 T0 = *reinterpret_cast<const uint2*>(perm + off0);
-            const uint2 T1 = *reinterpret_cast<const uint2*>(perm + off1);
+            const uint2 T0 = *reinterpret_cast<const uint2*>(tab_p + off0);
+            const uint2 T1 = *reinterpret_cast<const uint2*>(tab_p + off1);
             uint32_t v[8];
             if constexpr (kClassWords) {
               nib8_to_e4m3(q[r][blk].x, T0, v[0], v[1]);
@@ -749,8 +765,8 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
               nib8_natural_to_e4m3(q[r][blk].z, T1, v[4], v[5]);
               nib8_natural_to_e4m3(q[r][blk].w, T1, v[6], v[7]);
             }
-            st_shared_v4((bt + b_sw[r]) ^ ((2 * blk) << 4), v[0], v[1], v[2], v[3]);
-            st_shared_v4((bt + b_sw[r]) ^ ((2 * blk + 1) << 4), v[4], v[5], v[6], v[7]);
+            st_shared_v4(bt + b_off[2 * blk] + r * kBRowStep, v[0], v[1], v[2], v[3]);
+            st_shared_v4(bt + b_off[2 * blk + 1] + r * kBRowStep, v[4], v[5], v[6], v[7]);
           }
           // E8M0 bytes of the row's four 32-blocks (class words: bits 10..14 + 118)
           if constexpr (kClassWords)
