@@ -25,7 +25,7 @@ BD_ERR_DEVICE = -7
 BD_OUT_BF16, BD_OUT_F16, BD_OUT_F32 = 0, 1, 2
 BD_EPI_NONE, BD_EPI_BIAS, BD_EPI_BIAS_RELU, BD_EPI_BIAS_SILU, BD_EPI_BIAS_GELU = 0, 1, 2, 3, 4
 BD_SPLIT_REDUCE, BD_SPLIT_PLANES, BD_SPLIT_ATOMIC = 0, 1, 2
-BD_GEMM_OVERLAP_PREV, BD_GEMM_WEIGHTS_STATIC, BD_GEMM_B_E4M3 = 1, 2, 4
+BD_GEMM_OVERLAP_PREV, BD_GEMM_WEIGHTS_STATIC, BD_GEMM_B_E4M3, BD_GEMM_SINGLE_CTA = 1, 2, 4, 8
 BD_IN_F32, BD_IN_BF16 = 0, 1
 BD_DEVERR_WAIT_MASK, BD_DEVERR_WAIT_TMA, BD_DEVERR_NONFINITE, BD_DEVERR_RANGE = 0x1F, 0x01, 0x20, 0x40
 

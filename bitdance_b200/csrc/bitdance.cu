@@ -212,11 +212,22 @@ int launch_gemm(const GemmMaps& m, const GemmParams& p, int grid, bool overlap,
   cfg.blockDim = dim3(Cfg::kThreads);
   cfg.dynamicSmemBytes = Cfg::kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (overlap) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (Cfg::kPair) {  // clusters of two CTAs (grid is even)
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 2;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = overlap ? 1 : 0;
+  cfg.numAttrs = na;
   if (cudaLaunchKernelEx(&cfg, w4a6_gemm_kernel<BM, kClassWords>, m.a, m.as, m.w, m.ws, m.c, p) !=
       cudaSuccess)
     return BD_ERR_CUDA;
@@ -230,6 +241,7 @@ int launch_gemm_bm(int bm, const GemmMaps& m, const GemmParams& p, int grid, boo
     case 16: return launch_gemm<16, kClassWords>(m, p, grid, overlap, s);
     case 32: return launch_gemm<32, kClassWords>(m, p, grid, overlap, s);
     case 64: return launch_gemm<64, kClassWords>(m, p, grid, overlap, s);
+    case 256: return launch_gemm<256, kClassWords>(m, p, grid, overlap, s);
     default: return launch_gemm<128, kClassWords>(m, p, grid, overlap, s);
   }
 }
@@ -552,7 +564,7 @@ int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const ui
                     int K, int split_k, int split_mode, int out_dtype, int epilogue,
                     void* workspace, size_t workspace_bytes, unsigned flags, bd_stream_t stream) {
   if (flags & ~static_cast<unsigned>(BD_GEMM_OVERLAP_PREV | BD_GEMM_WEIGHTS_STATIC |
-                                     BD_GEMM_B_E4M3))
+                                     BD_GEMM_B_E4M3 | BD_GEMM_SINGLE_CTA))
     return BD_ERR_INVALID_ARG;
   if (!c || !a || !a_scales || !b || !b_scales) return BD_ERR_INVALID_ARG;
   if (out_dtype < BD_OUT_BF16 || out_dtype > BD_OUT_F32) return BD_ERR_INVALID_ARG;
@@ -574,13 +586,23 @@ int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const ui
   int st = device_info(&d);
   if (st != BD_OK) return st;
 
-  const int bm = token_tile(M);
-  const int m_tiles = (M + bm - 1) / bm, n_tiles = (N + kTileN - 1) / kTileN;
-  const int64_t tiles = static_cast<int64_t>(m_tiles) * n_tiles;
+  int bm = token_tile(M);
+  int m_tiles = (M + bm - 1) / bm;
+  int n_tiles = (N + kTileN - 1) / kTileN;
+  int64_t tiles = static_cast<int64_t>(m_tiles) * n_tiles;
   // split_k == 0: stream-K when the tiles do not fill the machine twice over, whole tiles
   // dealt round-robin otherwise (no fix-up needed); atomics never need the fix-up either
   const bool streamk = split_k == 0 && split_mode != BD_SPLIT_ATOMIC && tiles < 2 * d->sm_count;
   if (split_k == 0 && !streamk) split_k = 1;
+  // whole 128-token tiles, N % 256 == 0: tiles of 256 tokens computed by CTA pairs
+  const bool pair = bm == 128 && !streamk && split_k == 1 && split_mode != BD_SPLIT_ATOMIC &&
+                    N % 256 == 0 && !(flags & BD_GEMM_SINGLE_CTA) && d->sm_count >= 2;
+  if (pair) {
+    bm = 256;
+    m_tiles = (M + bm - 1) / bm;
+    tiles = static_cast<int64_t>(m_tiles) * n_tiles;
+  }
+  const int cta_rows = pair ? 128 : bm;  // token rows loaded per CTA
   const bool use_ws = split_k > 1 && split_mode == BD_SPLIT_REDUCE;
   StreamKSizes sk{0, 0, 0};
   if (streamk) {
@@ -597,10 +619,10 @@ int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const ui
   const int Mp4 = (M + 3) / 4 * 4;
   GemmMaps maps;
   if (!make_map_3d(&maps.a, CU_TENSOR_MAP_DATA_TYPE_UINT8, const_cast<uint8_t*>(a), 128, M, nkt,
-                   K, 128, 128, bm, 1, CU_TENSOR_MAP_SWIZZLE_128B))
+                   K, 128, 128, cta_rows, 1, CU_TENSOR_MAP_SWIZZLE_128B))
     return BD_ERR_CUDA;
   if (!make_map_2d(&maps.as, CU_TENSOR_MAP_DATA_TYPE_UINT32, const_cast<uint8_t*>(a_scales), Mp4,
-                   nkt, static_cast<uint64_t>(Mp4) * 4, bm, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
+                   nkt, static_cast<uint64_t>(Mp4) * 4, cta_rows, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
     return BD_ERR_CUDA;
   if (!make_map_2d(&maps.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, const_cast<uint8_t*>(b), 64,
                    static_cast<uint64_t>(N) * nkt, 64, 64, 128, CU_TENSOR_MAP_SWIZZLE_64B))
@@ -631,7 +653,7 @@ int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const ui
   // 32 outputs (64 B, the 64B swizzle span); the row pitch 2N is a multiple of 256 B
   std::memset(&maps.c, 0, sizeof(maps.c));
   p.tma_c = 0;
-  if (bm == 128 && split_mode != BD_SPLIT_ATOMIC && split_k <= 1 && out_dtype != BD_OUT_F32 &&
+  if (bm >= 128 && split_mode != BD_SPLIT_ATOMIC && split_k <= 1 && out_dtype != BD_OUT_F32 &&
       p.vec_out) {
     if (!make_map_2d(&maps.c, CU_TENSOR_MAP_DATA_TYPE_UINT16, c, N, M,
                      static_cast<uint64_t>(N) * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
@@ -653,7 +675,9 @@ int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const ui
     p.slots = static_cast<float*>(workspace);
     p.counters = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + sk.slots_bytes);
   }
-  const int grid = static_cast<int>(work < d->sm_count ? work : d->sm_count);
+  // pairs: one cluster of two CTAs per tile in flight, on pairs of SMs
+  const int64_t slots = pair ? d->sm_count / 2 : d->sm_count;
+  const int grid = static_cast<int>(work < slots ? work : slots) * (pair ? 2 : 1);
   const int rc = launch_gemm_any(bm, (flags & BD_GEMM_B_E4M3) == 0, maps, p, grid,
                                  (flags & BD_GEMM_OVERLAP_PREV) != 0,
                                  as_stream(stream));

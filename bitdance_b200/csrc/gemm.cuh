@@ -69,6 +69,9 @@ struct RingDepths {
   int sw, sb, st, groups;
 };
 constexpr RingDepths ring_depths(int BM) {
+  // CTA-pair tiles (BM = 256, 128 token rows and 128 weight rows per CTA): four slots of each
+  // ring, four groups of four warps (one weight row per thread)
+  if (BM == 256) return {4, 4, 4, 4};
   if (BM <= 16) return {4, 4, 4, 4};
   if (BM <= 32) return {4, 4, 4, 4};
   if (BM <= 64) return {4, 2, 6, 2};
@@ -78,9 +81,17 @@ constexpr RingDepths ring_depths(int BM) {
   return {2, 4, 2, 2};
 }
 
+// BM = 256: a tile of 256 token rows x 256 weight rows computed by a cluster of two CTAs with
+// the pair MMA (tcgen05 cta_group::2): CTA rank r loads, holds and stores token rows
+// 128 r .. 128 r + 127 of the tile, and loads and transcodes weight rows 128 r .. 128 r + 127
+// (the second operand of the MMA is split between the two CTAs' shared memory); rank 0 issues
+// the MMAs. Every weight chunk is transcoded once per 256 tokens instead of once per 128.
 template <int BM>
 struct GemmCfg {
   static constexpr int kBM = BM;
+  static constexpr bool kPair = BM == 256;
+  static constexpr int kRows = kPair ? 128 : BM;   // token rows per CTA
+  static constexpr int kBRows = kPair ? 128 : 256;  // weight rows per CTA (B operand rows)
   static constexpr int SW = ring_depths(BM).sw;
   static constexpr int SB = ring_depths(BM).sb;
   static constexpr int ST = ring_depths(BM).st;
@@ -88,7 +99,7 @@ struct GemmCfg {
   // weight stages released after their loads (guarded by a dependent store), token slots by
   // the epilogue warps after their copy into tensor memory; otherwise after the B rows are
   // stored and by the MMA's commit
-  static constexpr bool kEarlyRelease = BM == 128;
+  static constexpr bool kEarlyRelease = BM >= 128;
   // decode tiles: the transcode group that converted a chunk also writes the chunk's token rows
   // and scale factors into tensor memory and signals the MMA itself (one hand-off fewer per
   // chunk); 128-row tiles leave that to the epilogue warps (measured faster there)
@@ -96,15 +107,17 @@ struct GemmCfg {
   // token ring: BM rows x 128 B per slot (one E2M3 code per byte, 128B-swizzled so the copy
   // into tensor memory reads without bank conflicts), and the BM E8M0 words of each slot in a
   // separate small ring.
-  static constexpr int kTRowBytes = BM * 128;
-  static constexpr int kTScaleBytes = BM * 4;
+  static constexpr int kTRowBytes = kRows * 128;
+  static constexpr int kTScaleBytes = kRows * 4;
   static constexpr int kTScaleSlot = cround(kTScaleBytes, 128);  // TMA destinations: 128 B aligned
   static constexpr int kTTx = kTRowBytes + kTScaleBytes;
-  // weight stage: two 128-row halves x (8 KB codes, 64B-swizzled), then 2 x 1 KB scales
-  static constexpr int kWCodes = 16384;
-  static constexpr int kWStage = 16384 + 2048;
-  // B stage: 256 rows x 128 B E4M3 (128B-swizzled, K-major)
-  static constexpr int kBStage = 32768;
+  // weight stage: the CTA's 128-row halves x (8 KB codes, 64B-swizzled), then the 1 KB scale
+  // tiles of both halves of the tile (a CTA of a pair derives the peer half's E8M0 words too)
+  static constexpr int kWHalves = kBRows / 128;
+  static constexpr int kWCodes = 8192 * kWHalves;
+  static constexpr int kWStage = kWCodes + 2048;
+  // B stage: kBRows rows x 128 B E4M3 (128B-swizzled, K-major)
+  static constexpr int kBStage = kBRows * 128;
   static constexpr int oT = 0;
   static constexpr int oW = ST * kTRowBytes;
   static constexpr int oB = oW + SW * kWStage;
@@ -120,7 +133,7 @@ struct GemmCfg {
   static constexpr int oTs = oPerm + 64 * 8 * kPermCopies;  // token scale ring
   // 128-row tiles write C through shared memory with TMA stores (GemmParams::tma_c): per
   // epilogue warp two 2 KB staging buffers of 32 rows x 64 B (32 16-bit outputs), 64B-swizzled
-  static constexpr bool kTmaStore = BM == 128;
+  static constexpr bool kTmaStore = BM >= 128;
   static constexpr int kCStage = 2048;
   static constexpr int oC = kTmaStore ? cround(oTs + ST * kTScaleSlot, 1024) : oTs + ST * kTScaleSlot;
   static constexpr int oCtl = oC + (kTmaStore ? 4 * 2 * kCStage : 0);
@@ -138,14 +151,18 @@ struct GemmCfg {
   static constexpr int kTranscodeWarps = 16;
   static constexpr int kGroupWarps = kTranscodeWarps / kGroups;
   static_assert(kGroupWarps == 4 || kGroupWarps == 8, "delivery roles need four or eight warps");
-  static constexpr int kRowsPerThread = 256 / (32 * kGroupWarps);
+  static constexpr int kRowsPerThread = kBRows / (32 * kGroupWarps);
   static constexpr int kEpiWarps = 4;
   static constexpr int kTProducerWarp = 2 + kEpiWarps + kTranscodeWarps;  // 22
   static constexpr int kThreads = 32 * (kTProducerWarp + 1);
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static_assert(kSfCol0 + SB * kSfCols <= kTmemCols, "tensor memory budget");
   static_assert(kSfCols % 4 == 0 && kSfCol0 % 4 == 0, "scale-factor addresses 4-column aligned");
-  static_assert(oW % 1024 == 0 && oB % 1024 == 0 && kTRowBytes % 1024 == 0, "1 KB swizzle atoms");
+  static_assert(oW % 1024 == 0 && oB % 1024 == 0 && kTRowBytes % 1024 == 0 &&
+                    kWStage % 1024 == 0 && kBStage % 1024 == 0,
+                "1 KB swizzle atoms");
+  static_assert(kRowsPerThread >= 1, "a weight row per thread at least");
+  static_assert(!kPair || kRowsPerThread == 1, "pairs: one weight row per thread");
   static_assert(oTs % 128 == 0 && kTScaleSlot % 128 == 0 && kWCodes % 128 == 0,
                 "TMA shared-memory destinations 128-byte aligned");
   static_assert(!kTmaStore || oC % 1024 == 0, "64B-swizzled staging buffers 1 KB aligned");
@@ -458,7 +475,7 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
 template <class Cfg>
 __device__ __forceinline__ void copy_token_rows(const uint8_t* smem, int ts, int mrow, uint32_t dst) {
   uint32_t av[32];
-  if (mrow < Cfg::kBM) {
+  if (mrow < Cfg::kRows) {
     const uint8_t* trow =
         smem + Cfg::oT + ts * Cfg::kTRowBytes + (mrow >> 3) * 1024 + (mrow & 7) * 128;
 #pragma unroll
@@ -492,10 +509,16 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
   GemmCtl& ctl = *reinterpret_cast<GemmCtl*>(smem + Cfg::oCtl);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int cta = blockIdx.x;
+  // CTA pairs: the schedule deals tiles to clusters; `rank` picks this CTA's token and weight
+  // rows of the tile
+  const uint32_t rank = Cfg::kPair ? cluster_ctarank() : 0u;
+  const int cta = Cfg::kPair ? static_cast<int>(blockIdx.x / 2) : static_cast<int>(blockIdx.x);
   volatile uint32_t* abort_flag = &ctl.abort_flag;
   Schedule sch;
-  sch.init(p, gridDim.x);
+  sch.init(p, Cfg::kPair ? gridDim.x / 2 : gridDim.x);
+  // pair barriers the peer CTA arrives on, as shared::cluster addresses in rank 0 (bready,
+  // acc_empty) and in the peer (sfready)
+  const uint32_t peer = rank ^ 1u;
 
   if (tid == 0) {
     ctl.abort_flag = 0;
@@ -507,18 +530,24 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
       mbar_init(smem_u32(&ctl.tfull[s]), 1);
       mbar_init(smem_u32(&ctl.tempty[s]), Cfg::kEarlyRelease ? Cfg::kEpiWarps : 1);
     }
+    // pairs: bready and acc_empty of rank 0 count both CTAs' epilogue warps, sfready of each
+    // CTA both CTAs' transcode groups; the commits of the pair MMAs arrive once in each CTA
+    constexpr int kPairs = Cfg::kPair ? 2 : 1;
     for (int s = 0; s < Cfg::SB; ++s) {
-      mbar_init(smem_u32(&ctl.bready[s]), Cfg::kGroupDelivers ? Cfg::kGroupWarps : Cfg::kEpiWarps);
+      mbar_init(smem_u32(&ctl.bready[s]),
+                Cfg::kGroupDelivers ? Cfg::kGroupWarps : kPairs * Cfg::kEpiWarps);
       mbar_init(smem_u32(&ctl.bempty[s]), 1);
       mbar_init(smem_u32(&ctl.sfready[s]), Cfg::kGroupWarps);
     }
     mbar_init(smem_u32(&ctl.acc_full), 1);
-    mbar_init(smem_u32(&ctl.acc_empty), Cfg::kEpiWarps);
+    mbar_init(smem_u32(&ctl.acc_empty), kPairs * Cfg::kEpiWarps);
     mbar_init(smem_u32(&ctl.drain), 1);
     mbar_init(smem_u32(&ctl.fin_bar), 1);
     fence_mbar_init();
   }
   __syncthreads();
+  // the peer arrives on these barriers: both CTAs' are initialised before anyone arrives
+  if constexpr (Cfg::kPair) cluster_sync_all();
   // a grid launched after this one with programmatic serialisation may be scheduled now; it
   // takes this SM only after this CTA exits, and waits for this grid before it reads A or
   // touches C and the workspace
@@ -529,8 +558,13 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
   uint32_t tbase = 0;
   if (warp >= 1 && warp < Cfg::kTProducerWarp) {
     if (warp == 1) {
-      tmem_alloc(smem_u32(&ctl.tmem_base), Cfg::kTmemCols);
-      tmem_relinquish();
+      if constexpr (Cfg::kPair) {
+        tmem_alloc_pair(smem_u32(&ctl.tmem_base), Cfg::kTmemCols);
+        tmem_relinquish_pair();
+      } else {
+        tmem_alloc(smem_u32(&ctl.tmem_base), Cfg::kTmemCols);
+        tmem_relinquish();
+      }
     } else if (warp >= 2 + Cfg::kEpiWarps) {
       const int t0 = tid - 32 * (2 + Cfg::kEpiWarps);
       if constexpr (!kClassWords) load_tables<true>(ctl.tab, t0, 32 * Cfg::kTranscodeWarps);
@@ -555,10 +589,14 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
       Seg sg;
       for (int idx = 0; sch.segment(cta, idx, sg) && !*abort_flag; ++idx) {
         const int nt = sg.tile % p.n_tiles;
-        // the second 128-row half is missing in the last tile when N / 128 is odd
-        const bool two = 2 * nt + 1 < p.n_half_tiles;
-        const uint32_t tx = two ? Cfg::kWStage : Cfg::kWStage / 2;
-        int row0 = (2 * nt) * p.nks + sg.k0;  // (half tile, chunk) row of the packed weights
+        // the second 128-row half is missing in the last tile when N / 128 is odd (pair tiles
+        // need N % 256 == 0: each CTA loads its own half)
+        const bool two = !Cfg::kPair && 2 * nt + 1 < p.n_half_tiles;
+        const uint32_t tx = (two || Cfg::kPair) ? Cfg::kWStage : Cfg::kWStage / 2;
+        // (half tile, chunk) row of the packed weights: the tile's first half; a CTA of a pair
+        // loads the codes of its own half and the scales of both
+        int row0 = (2 * nt) * p.nks + sg.k0;
+        const int own = static_cast<int>(rank) * p.nks;
         for (int k = sg.k0; k < sg.k1; ++k, ++row0) {
           if (!mbar_wait(smem_u32(&ctl.wempty[w.slot]), w.phase ^ 1u, p.err, kErrWaitEmpty,
                          abort_flag))
@@ -566,12 +604,11 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
           uint8_t* st = smem + Cfg::oW + w.slot * Cfg::kWStage;
           const uint32_t fb = smem_u32(&ctl.wfull[w.slot]);
           mbar_arrive_expect_tx(fb, tx);
-          tma_load_2d(smem_u32(st), &tm_w, 0, row0 * 128, fb);
+          tma_load_2d(smem_u32(st), &tm_w, 0, (row0 + own) * 128, fb);
           tma_load_2d(smem_u32(st + Cfg::kWCodes), &tm_ws, 0, row0, fb);
-          if (two) {
-            tma_load_2d(smem_u32(st + 8192), &tm_w, 0, (row0 + p.nks) * 128, fb);
+          if (two || Cfg::kPair)
             tma_load_2d(smem_u32(st + Cfg::kWCodes + 1024), &tm_ws, 0, row0 + p.nks, fb);
-          }
+          if (two) tma_load_2d(smem_u32(st + 8192), &tm_w, 0, (row0 + p.nks) * 128, fb);
           w.next();
         }
       }
@@ -593,28 +630,33 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
           uint8_t* st = smem + Cfg::oT + t.slot * Cfg::kTRowBytes;
           const uint32_t fb = smem_u32(&ctl.tfull[t.slot]);
           mbar_arrive_expect_tx(fb, Cfg::kTTx);
-          tma_load_3d(smem_u32(st), &tm_a, 0, mt * BM, k, fb);
-          tma_load_2d(smem_u32(smem + Cfg::oTs + t.slot * Cfg::kTScaleSlot), &tm_as, mt * BM, k,
-                      fb);
+          const int m0 = mt * BM + static_cast<int>(rank) * Cfg::kRows;
+          tma_load_3d(smem_u32(st), &tm_a, 0, m0, k, fb);
+          tma_load_2d(smem_u32(smem + Cfg::oTs + t.slot * Cfg::kTScaleSlot), &tm_as, m0, k, fb);
           t.next();
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // (pairs: rank 0 issues for both CTAs, its commits arrive in both)
+    if (lane == 0 && rank == 0) {
+      auto commit = [&](uint64_t& bar) {
+        if constexpr (Cfg::kPair) tc_commit_pair(smem_u32(&bar), 3);
+        else tc_commit(smem_u32(&bar));
+      };
       RingPos<Cfg::SB> b;
       RingPos<Cfg::ST> t;
       Seg sg;
       for (int idx = 0; sch.segment(cta, idx, sg); ++idx) {
         if (!mbar_wait(smem_u32(&ctl.acc_empty), (idx & 1) ^ 1u, p.err, kErrWaitAccum,
-                            abort_flag))
+                       abort_flag))
           break;
         tc_fence_after();
         bool ok = true;
         for (int k = sg.k0; k < sg.k1; ++k) {
           // bready: the B tile, its scales and the token operand (copied into tensor memory
-          // after the token slot landed) are all in place
+          // after the token slot landed) are all in place (in both CTAs of a pair)
           if (!mbar_wait(smem_u32(&ctl.bready[b.slot]), b.phase, p.err, kErrWaitOperand,
                          abort_flag)) {
             ok = false;
@@ -626,20 +668,27 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
           const uint32_t sfa = tbase + Cfg::kSfCol0 + b.slot * Cfg::kSfCols;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t idesc = idesc_mxf8f6f4(128, kTileN, kFmtE2M3, kFmtE4M3, kk, kk);
-            mma_mxf8f6f4_ts(tbase, ta + kk * 8, sdesc_sw128(b_addr + kk * 32), idesc, sfa, sfa + 4,
-                            (k == sg.k0 && kk == 0) ? 0u : 1u);
+            const uint32_t acc = (k == sg.k0 && kk == 0) ? 0u : 1u;
+            if constexpr (Cfg::kPair) {
+              const uint32_t idesc = idesc_mxf8f6f4(256, kTileN, kFmtE2M3, kFmtE4M3, kk, kk);
+              mma_mxf8f6f4_ts_pair(tbase, ta + kk * 8, sdesc_sw128(b_addr + kk * 32), idesc, sfa,
+                                   sfa + 4, acc);
+            } else {
+              const uint32_t idesc = idesc_mxf8f6f4(128, kTileN, kFmtE2M3, kFmtE4M3, kk, kk);
+              mma_mxf8f6f4_ts(tbase, ta + kk * 8, sdesc_sw128(b_addr + kk * 32), idesc, sfa,
+                              sfa + 4, acc);
+            }
           }
-          tc_commit(smem_u32(&ctl.bempty[b.slot]));
-          if constexpr (!Cfg::kEarlyRelease) tc_commit(smem_u32(&ctl.tempty[t.slot]));
+          commit(ctl.bempty[b.slot]);
+          if constexpr (!Cfg::kEarlyRelease) commit(ctl.tempty[t.slot]);
           b.next();
           t.next();
         }
-        tc_commit(smem_u32(&ctl.acc_full));
+        commit(ctl.acc_full);
         if (!ok) break;
       }
       // arrives once every tcgen05 operation this thread issued has completed
-      tc_commit(smem_u32(&ctl.drain));
+      commit(ctl.drain);
     }
   } else if (warp >= 2 + Cfg::kEpiWarps) {
     // ------------------------------------------------------------------ transcode
@@ -661,7 +710,7 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
       // the row offset has zero bits 4..5 and the stage base is 1 KB aligned, so the address
       // of chunk c is (stage + row offset + swizzle << 4) ^ (c << 4)
       code_sw[r] = (row >> 7) * 8192 + rr * 64 + (((rr >> 1) & 3) << 4);
-      scale_off[r] = Cfg::kWCodes + (row >> 7) * 1024 + rr * 8;
+      scale_off[r] = Cfg::kWCodes + ((row >> 7) + static_cast<int>(rank)) * 1024 + rr * 8;
       // B operand: 128B-swizzled K-major, 16-byte chunk cc of row n at
       // (n >> 3)*1024 + (n & 7)*128 + ((cc ^ (n & 7)) << 4); block b covers chunks 2b, 2b + 1
       // likewise bits 4..6: chunk cc of row n at (slot + row offset + ((n & 7) << 4)) ^ (cc << 4)
@@ -699,12 +748,18 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
           for (int c = 0; c < 4; ++c) q[r][c] = ld_shared_v4(st_u + code_off[c] + r * kCodeRowStep);
           sc[r] = *reinterpret_cast<const uint2*>(st + scale_off[0] + r * kScaleRowStep);
         }
+        // pairs: the peer half's class words of this thread's row (for its E8M0 word), loaded
+        // with the rest before the stage is released
+        uint2 sp = make_uint2(0u, 0u);
+        if constexpr (Cfg::kPair)
+          sp = *reinterpret_cast<const uint2*>(st + Cfg::kWCodes + static_cast<int>(peer) * 1024 +
+                                               rows[0] * 8);
         if constexpr (Cfg::kEarlyRelease) {
           // Release the weight stage now: a store that depends on every load (never taken, but
           // the loads must complete before it can issue; one word of a vector load completes
           // with the others) comes before the arrive, so no load of the stage is pending when
           // its next TMA fill lands.
-          uint32_t dep = 0;
+          uint32_t dep = sp.x;
 #pragma unroll
           for (int r = 0; r < R; ++r) {
             dep ^= sc[r].x;
@@ -772,7 +827,25 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
           if constexpr (kClassWords)
             sfw = prmt((sc[r].x >> 10) & 0x001F001Fu, (sc[r].y >> 10) & 0x001F001Fu, 0x6420u) +
                   0x76767676u;
-          sf_stage[rows[r]] = sfw;
+          sf_stage[static_cast<int>(rank) * Cfg::kBRows + rows[r]] = sfw;
+          if constexpr (Cfg::kPair) {
+            // each CTA's MMA reads the scales of all 256 weight rows from its own tensor memory:
+            // the E8M0 words of the peer half's row too (R == 1 in pairs)
+            uint32_t sfp = 0;
+            if constexpr (kClassWords) {
+              sfp = prmt((sp.x >> 10) & 0x001F001Fu, (sp.y >> 10) & 0x001F001Fu, 0x6420u) +
+                    0x76767676u;
+            } else {
+#pragma unroll
+              for (int blk = 0; blk < 4; ++blk) {
+                const uint32_t f = blk < 2 ? (sp.x >> (16 * blk)) : (sp.y >> (16 * (blk - 2)));
+                uint32_t i0, i1, e8;
+                pair_class(ctl.tab, f & 0xFFu, (f >> 8) & 0xFFu, i0, i1, e8);
+                sfp |= e8 << (8 * blk);
+              }
+            }
+            sf_stage[static_cast<int>(peer) * Cfg::kBRows + rows[r]] = sfp;
+          }
         }
         fence_proxy_async_smem();  // the tensor core reads the B tile through the async proxy
         __syncwarp();
@@ -868,10 +941,11 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
           ok = false;
           break;
         }
-        if (quarter * 32 < BM) copy_token_rows<Cfg>(smem, t.slot, mrow, taddr + Cfg::kACol0 + b.slot * 32);
+        if (quarter * 32 < Cfg::kRows)
+          copy_token_rows<Cfg>(smem, t.slot, mrow, taddr + Cfg::kACol0 + b.slot * 32);
         const uint32_t* tok = reinterpret_cast<const uint32_t*>(
             smem + Cfg::oTs + t.slot * Cfg::kTScaleSlot);
-        const uint32_t tokw = mrow < BM ? tok[mrow] : 0u;
+        const uint32_t tokw = mrow < Cfg::kRows ? tok[mrow] : 0u;
         if constexpr (Cfg::kEarlyRelease) {
           // the token rows went to tensor memory from registers and the scale is in a
           // register: the token slot can be refilled
@@ -889,7 +963,10 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&ctl.bready[b.slot]));
+        if (lane == 0) {
+          if (Cfg::kPair && rank != 0) mbar_arrive_remote(mapa_shared(smem_u32(&ctl.bready[b.slot]), 0));
+          else mbar_arrive(smem_u32(&ctl.bready[b.slot]));
+        }
         b.next();
         t.next();
       }
@@ -898,9 +975,10 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         break;
       tc_fence_after();
       const int mt = sg.tile / p.n_tiles, nt = sg.tile % p.n_tiles;
-      const int m0 = mt * BM, n0 = nt * kTileN;
-      const int mrows = min(BM, p.M - m0);       // valid token rows of this tile
-      const int ncols = min(kTileN, p.N - n0);   // valid weight rows (multiple of 128)
+      // this CTA's token rows of the tile (pairs: rank r holds rows 128 r ..)
+      const int m0 = mt * BM + static_cast<int>(rank) * Cfg::kRows, n0 = nt * kTileN;
+      const int mrows = min(Cfg::kRows, p.M - m0);  // valid token rows (may be <= 0 in a pair)
+      const int ncols = min(kTileN, p.N - n0);      // valid weight rows (multiple of 128)
       const bool warp_rows = quarter * 32 < mrows;
       const bool row_ok = mrow < mrows;
       const int m = m0 + mrow;
@@ -927,7 +1005,10 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&ctl.acc_empty));
+        if (lane == 0) {
+          if (Cfg::kPair && rank != 0) mbar_arrive_remote(mapa_shared(smem_u32(&ctl.acc_empty), 0));
+          else mbar_arrive(smem_u32(&ctl.acc_empty));
+        }
         if (p.fixup_kernel) continue;  // summed after this grid by streamk_fixup_kernel
         __threadfence();
         const int first = sch.cta_of(sg.tile * p.nks);
@@ -1006,7 +1087,10 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
           }
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&ctl.acc_empty));
+          if (lane == 0) {
+            if (Cfg::kPair && rank != 0) mbar_arrive_remote(mapa_shared(smem_u32(&ctl.acc_empty), 0));
+            else mbar_arrive(smem_u32(&ctl.acc_empty));
+          }
           continue;
         }
       }
@@ -1049,7 +1133,10 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&ctl.acc_empty));
+      if (lane == 0) {
+        if (Cfg::kPair && rank != 0) mbar_arrive_remote(mapa_shared(smem_u32(&ctl.acc_empty), 0));
+        else mbar_arrive(smem_u32(&ctl.acc_empty));
+      }
     }
     // this warp's TMA stores of C complete before the grid does
     if (Cfg::kTmaStore && c_stores > 0 && lane == 0) bulk_wait_group_all();
@@ -1060,11 +1147,18 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
-    // tensor memory is freed only after every MMA the MMA thread issued is done
+    // tensor memory is freed only after every MMA the MMA thread issued is done (pairs: rank
+    // 0's last commit arrives in both CTAs)
     if (lane == 0) mbar_wait(smem_u32(&ctl.drain), 0, p.err, kErrWaitMma, nullptr);
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tbase, Cfg::kTmemCols);
+    if constexpr (!Cfg::kPair) tmem_dealloc(tbase, Cfg::kTmemCols);
+  }
+  if constexpr (Cfg::kPair) {
+    // neither CTA frees its tensor memory or exits while the peer may still arrive on its
+    // barriers or store into its shared memory
+    cluster_sync_all();
+    if (warp == 1) tmem_dealloc_pair(tbase, Cfg::kTmemCols);
   }
 }
 

@@ -78,18 +78,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// The same with acquire semantics at cluster scope: for barriers the peer CTA of a pair
+// arrives on (its arrive releases its writes at cluster scope).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait on phase `parity`. After `limit` SM cycles ORs `code` into *err, sets
 // *abort_flag and returns false. Also returns false early if another role already aborted.
 // The hot path is a tight try_wait loop (try_wait itself suspends the thread in hardware for
 // a while); the abort flag and the cycle counter are looked at only every 1024 tries.
+// kCluster: acquire at cluster scope (mbar_try_wait_cluster).
+template <bool kCluster = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t* err,
                                           uint32_t code, volatile uint32_t* abort_flag,
                                           unsigned long long limit = kWaitLimitCycles) {
-  if (mbar_try_wait(bar, parity)) return true;
+  auto try_once = [&]() {
+    return kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+  };
+  if (try_once()) return true;
   const long long t0 = clock64();
   uint32_t spins = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (try_once()) return true;
     if ((++spins & 1023u) == 0) {
       if (abort_flag != nullptr && *abort_flag) return false;
       if (static_cast<unsigned long long>(clock64() - t0) > limit) {
@@ -116,6 +134,38 @@ struct RingPos {
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------------
+// CTA pairs (clusters of two): rank in the cluster, a barrier over both CTAs, addresses in
+// the peer's shared memory, stores and mbarrier arrives there
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// every thread of both CTAs (warp-converged)
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cluster address of the same shared-memory location in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+// arrive on an mbarrier given by its shared::cluster address (this CTA's or the peer's), with
+// the default semantics (release at CTA scope): what the waiter needs ordered before it is
+// tensor-memory writes, completed by tcgen05.wait::st and fenced by
+// tcgen05.fence::before_thread_sync before the arrive (a release at cluster scope made every
+// arrive wait about a microsecond)
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 
 // ---------------------------------------------------------------------------------
@@ -184,6 +234,20 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
                : "memory");
 }
+// tensor memory of a CTA pair (the MMAs of cta_group::2 write both CTAs' allocations at the
+// same address): executed by the same warp of both CTAs
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -194,6 +258,15 @@ __device__ __forceinline__ void tc_fence_after() {
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      : "memory");
+}
+// The same for the MMAs of a CTA pair, arriving on the barrier at `bar` in every CTA of
+// `cta_mask` (bit r: CTA rank r of the cluster).
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
       : "memory");
 }
 // Shared -> tensor memory: 32 rows x 16 bytes, replicated into all four lane quarters.
@@ -328,6 +401,21 @@ __device__ __forceinline__ void mma_mxf8f6f4_ss(uint32_t d_tmem, uint64_t adesc,
       "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::
           "r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+// MMA of a CTA pair (M = 256: rows 0..127 in CTA rank 0, 128..255 in rank 1; B's N rows split
+// in halves the same way; D, A and the A scales in each CTA's own tensor memory, the B scales
+// of all N rows in each), A from tensor memory, issued by rank 0.
+__device__ __forceinline__ void mma_mxf8f6f4_ts_pair(uint32_t d_tmem, uint32_t a_tmem,
+                                                     uint64_t bdesc, uint32_t idesc,
+                                                     uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], [%1], %2, %3, [%5], [%6], p;\n\t}\n" ::
+          "r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
       : "memory");
 }
 // Same with the A operand read from tensor memory.

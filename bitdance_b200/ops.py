@@ -280,14 +280,16 @@ def w4a6_gemm(acts: PackedActivations, weights: PackedWeights,
               epilogue: str = "none", split_k: int = 0, split_mode: str = "reduce",
               out: Optional[torch.Tensor] = None, workspace=None,
               stream=None, overlap_prev: bool = False,
-              weights_static: bool = False) -> torch.Tensor:
+              weights_static: bool = False, single_cta: bool = False) -> torch.Tensor:
     """C[M, N] = A . B^T * tensor_scale (+ bias, activation) on the tensor cores.
 
     split_k=0 (default) runs the persistent stream-K schedule; its scratch comes from
     `workspace` (a zeroed uint8 tensor or a Workspace), else from a per-stream Workspace.
     overlap_prev: the kernel may be scheduled while the previous kernel on the stream
     finishes (it waits for it before reading A/bias or writing C). weights_static (with
-    overlap_prev): the previous kernel does not write the weights, so they stream early."""
+    overlap_prev): the previous kernel does not write the weights, so they stream early.
+    single_cta: no CTA-pair tiles (large GEMMs otherwise compute 256-token tiles on pairs of
+    CTAs sharing each MMA; same results)."""
     M, K, N = acts.M, acts.K, weights.N
     if weights.K != K:
         raise ValueError(f"K mismatch: activations {K}, weights {weights.K}")
@@ -311,7 +313,8 @@ def w4a6_gemm(acts: PackedActivations, weights: PackedWeights,
         raise ValueError(f"epilogue {epilogue!r} needs a bias")
     flags = (_lib.BD_GEMM_OVERLAP_PREV if overlap_prev else 0) | \
         (_lib.BD_GEMM_WEIGHTS_STATIC if weights_static else 0) | \
-        (_lib.BD_GEMM_B_E4M3 if weights.sideband == "e4m3" else 0)
+        (_lib.BD_GEMM_B_E4M3 if weights.sideband == "e4m3" else 0) | \
+        (_lib.BD_GEMM_SINGLE_CTA if single_cta else 0)
     call("bd_w4a6_gemm_ex", _p(out), _p(acts.codes), _p(acts.scales), _p(weights.codes),
          _p(weights.scales), float(weights.tensor_scale), _p(bias), M, N, K, split_k,
          SPLIT_MODES[split_mode], _OUT[out_dtype], epi, _p(workspace),

@@ -226,6 +226,7 @@ int bd_w4a6_gemm(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8
 #define BD_GEMM_OVERLAP_PREV 1u   /* may start while the previous kernel on the stream ends */
 #define BD_GEMM_WEIGHTS_STATIC 2u /* b / b_scales are not written by that previous kernel */
 #define BD_GEMM_B_E4M3 4u         /* b / b_scales in the E4M3-sideband layout (bd_pack_b_e4m3) */
+#define BD_GEMM_SINGLE_CTA 8u     /* no CTA-pair tiles (one CTA per 128-token tile throughout) */
 
 /* bd_w4a6_gemm with launch flags (same arguments, same results). BD_GEMM_B_E4M3: b and b_scales
  * are in the E4M3-sideband layout (bd_pack_b_e4m3) instead of bd_pack_b's; same results for the
@@ -237,7 +238,11 @@ int bd_w4a6_gemm(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8
  * c or the workspace. With BD_GEMM_WEIGHTS_STATIC as well, it starts streaming b and
  * b_scales before that wait, so the caller guarantees that the previous kernel does not
  * write them (weights that stay resident across decode steps). No reference counterpart: the
- * reference launches each GEMM on its own (kernel/bench_sweep.py:87-161). */
+ * reference launches each GEMM on its own (kernel/bench_sweep.py:87-161).
+ * Where whole tiles of 128 tokens fill the machine twice over and N % 256 == 0, tiles of 256
+ * tokens x 256 weight rows are computed by clusters of two CTAs sharing each MMA (each CTA
+ * transcodes half of every weight chunk); BD_GEMM_SINGLE_CTA keeps one CTA per 128-token tile
+ * (same results, bit for bit). */
 int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const uint8_t* b,
                     const uint8_t* b_scales, float b_tensor_scale, const void* bias, int M, int N,
                     int K, int split_k, int split_mode, int out_dtype, int epilogue,

@@ -45,7 +45,7 @@ int main(void) {
          BD_ERR_ALIGNMENT);
   expect("gemm_ex: unknown flag",
          bd_w4a6_gemm_ex(ok, u8, u8, u8, u8, 1.0f, NULL, 16, 128, 128, 1, BD_SPLIT_REDUCE,
-                         BD_OUT_BF16, BD_EPI_NONE, NULL, 0, 8u, NULL),
+                         BD_OUT_BF16, BD_EPI_NONE, NULL, 0, 16u, NULL),
          BD_ERR_INVALID_ARG);
   expect("noalloc: bias epilogue without bias",
          bd_w4a6_gemm_noalloc(ok, u8, u8, u8, u8, 1.0f, NULL, 16, 128, 128, BD_OUT_BF16,

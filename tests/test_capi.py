@@ -70,9 +70,10 @@ def test_gemm_ex_validates_flags_then_arguments(lib):
     ok = P(4096)
     g = lib.bd_w4a6_gemm_ex
     # unknown flag bit
-    assert g(ok, ok, ok, ok, ok, 1.0, None, 16, 128, 128, 1, 0, 0, 0, None, 0, 8, None) == -1
-    # known flags (BD_GEMM_B_E4M3 = 4 among them), then the same checks as bd_w4a6_gemm
-    assert g(None, ok, ok, ok, ok, 1.0, None, 16, 128, 128, 1, 0, 0, 0, None, 0, 7, None) == -1
+    assert g(ok, ok, ok, ok, ok, 1.0, None, 16, 128, 128, 1, 0, 0, 0, None, 0, 16, None) == -1
+    # known flags (BD_GEMM_B_E4M3 = 4, BD_GEMM_SINGLE_CTA = 8 among them), then the same checks
+    # as bd_w4a6_gemm
+    assert g(None, ok, ok, ok, ok, 1.0, None, 16, 128, 128, 1, 0, 0, 0, None, 0, 15, None) == -1
     assert g(ok, ok, ok, ok, ok, 1.0, None, 16, 100, 128, 1, 0, 0, 0, None, 0, 1, None) == -2
 
 

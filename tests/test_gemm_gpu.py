@@ -392,3 +392,35 @@ def test_token_tiles_of_128_rows_store_paths(M, out_dtype, epi):
     g = got.float().cpu().numpy().astype(np.float64)
     assert o.rel_linf(C, g) <= TOL_REL_LINF
     assert torch.equal(got, odd)
+
+
+@pytest.mark.parametrize("M,N,K,out_dtype,epi,sideband", [
+    (2400, 4096, 512, torch.bfloat16, "none", "class"),      # last pair tile: rank 1 has no rows
+    (2440, 4096, 256, torch.float16, "bias_gelu", "class"),  # rank 1 holds 8 rows of the last tile
+    (2560, 4096, 128, torch.float32, "bias", "class"),       # one chunk per tile; fp32 C (no TMA store)
+    (2432, 4096, 384, torch.bfloat16, "bias_relu", "e4m3"),  # E4M3 sideband
+])
+def test_cta_pair_tiles(M, N, K, out_dtype, epi, sideband):
+    """Whole tiles that fill the machine twice over run as 256-token tiles on CTA pairs (the
+    pair MMA, each CTA transcoding half of every weight chunk): against the oracle, and the same
+    bits as the single-CTA schedule (BD_GEMM_SINGLE_CTA)."""
+    import bitdance_b200 as bd
+    ops = random_operands(M, N, K, seed=M + K, b_scale_lo=0x18, b_scale_hi=0x30)
+    bias = (np.random.default_rng(K).standard_normal(N) * 2).astype(np.float32)
+    bias_bf = torch.from_numpy(bias).to(torch.bfloat16)
+    C, Cabs = gold(*ops, 0.05, bias_bf.float().numpy().astype(np.float64) if epi != "none" else None)
+    if epi == "bias_relu":
+        C = np.maximum(C, 0)
+    elif epi == "bias_gelu":
+        C = 0.5 * C * (1 + np.tanh(0.7978845608028654 * (C + 0.044715 * C ** 3)))
+    acts = bd.pack_activations(dev(ops[0]), dev(ops[1]))
+    w = bd.pack_weights(dev(ops[2]), dev(ops[3]), 0.05, sideband=sideband)
+    kw = dict(out_dtype=out_dtype, epilogue=epi, bias=bias_bf.cuda() if epi != "none" else None)
+    pair = bd.w4a6_gemm(acts, w, **kw)
+    single = bd.w4a6_gemm(acts, w, single_cta=True, **kw)
+    torch.cuda.synchronize()
+    assert bd.device_error() == 0
+    g = pair.float().cpu().numpy().astype(np.float64)
+    assert np.isfinite(g).all()
+    assert o.rel_linf(C, g) <= TOL_REL_LINF
+    assert torch.equal(pair, single)
