@@ -700,17 +700,21 @@ def run_ours(args, rank, world, local_rank):
             raise RuntimeError(f"kernel error word 0x{w:x} set after {stage}")
 
     no_device_error("the decode sweep")
-    # tensor peak of the block-scaled MMA, measured now (SS and TS operand forms)
+    # tensor peak of the block-scaled MMA, measured now (SS and TS operand forms, and the
+    # CTA-pair MMA of the large GEMMs' tiles); the roofline takes the fastest
     probe = None
     tensor_peak, tensor_kind = 2.0 * peaks["bf16_tflops"], "2x measured cuBLAS bf16 burst"
     if not args.no_configs:
         try:
             ss = ops.mma_peak_tflops(n_cols=256, a_from_tmem=False)
             ts = ops.mma_peak_tflops(n_cols=256, a_from_tmem=True)
-            probe = {"ss_tflops": ss, "ts_tflops": ts,
-                     "what": "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale M=128 N=256 "
-                             "K=32, one CTA per SM, back to back (bd_probe_mma_peak)"}
-            tensor_peak, tensor_kind = max(ss, ts), "measured by the MMA probe (this run)"
+            pair = ops.mma_peak_tflops(pair=True)
+            probe = {"ss_tflops": ss, "ts_tflops": ts, "pair_tflops": pair,
+                     "what": "tcgen05.mma.kind::mxf8f6f4.block_scale N=256 K=32 back to back, "
+                             "pseudo-random operands: cta_group::1 M=128 one CTA per SM (A in "
+                             "shared or tensor memory), cta_group::2 M=256 one cluster per two "
+                             "SMs (bd_probe_mma_peak)"}
+            tensor_peak, tensor_kind = max(ss, ts, pair), "measured by the MMA probe (this run)"
         except Exception as e:  # noqa: BLE001 - report, keep the fallback
             probe = {"error": repr(e)}
 
@@ -811,6 +815,7 @@ def run_case(args):
             for tm in (False, True):
                 res[f"N{n}_{'ts' if tm else 'ss'}_tflops"] = ops.mma_peak_tflops(
                     n_cols=n, a_from_tmem=tm, mmas_per_cta=args.steps * 64)
+        res["N256_pair_tflops"] = ops.mma_peak_tflops(pair=True, mmas_per_cta=args.steps * 64)
         print(json.dumps(res), flush=True)
         return 0
     if args.case == "gemm":

@@ -312,6 +312,8 @@ int bd_selftest_bounded_wait(int64_t limit_cycles, bd_stream_t stream) {
 int bd_probe_mma_peak(int64_t mmas_per_cta, int n_cols, int a_from_tmem, bd_stream_t stream) {
   if (mmas_per_cta < 1 || mmas_per_cta > (int64_t{1} << 21)) return BD_ERR_INVALID_ARG;
   if (n_cols < 16 || n_cols > 256 || n_cols % 16) return BD_ERR_INVALID_ARG;
+  if (a_from_tmem < 0 || a_from_tmem > 2 || (a_from_tmem == 2 && n_cols != 256))
+    return BD_ERR_INVALID_ARG;
   DeviceInfo* d = nullptr;
   int st = device_info(&d);
   if (st != BD_OK) return st;
@@ -321,9 +323,29 @@ int bd_probe_mma_peak(int64_t mmas_per_cta, int n_cols, int a_from_tmem, bd_stre
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load() & bit)) {
     if (cudaFuncSetAttribute(mma_peak_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kProbeSmem) != cudaSuccess ||
+        cudaFuncSetAttribute(mma_peak_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kProbeSmem) != cudaSuccess)
       return BD_ERR_CUDA;
     configured.fetch_or(bit);
+  }
+  if (a_from_tmem == 2) {  // CTA pairs: one cluster of two CTAs per pair of SMs
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(d->sm_count / 2 * 2));
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = kProbeSmem;
+    cfg.stream = as_stream(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, mma_peak_pair_kernel, static_cast<long long>(mmas_per_cta),
+                           d->err) != cudaSuccess)
+      return BD_ERR_CUDA;
+    return cudaPeekAtLastError() == cudaSuccess ? BD_OK : BD_ERR_CUDA;
   }
   mma_peak_kernel<<<d->sm_count, 128, kProbeSmem, as_stream(stream)>>>(
       static_cast<long long>(mmas_per_cta), n_cols, a_from_tmem ? 1 : 0, d->err);

@@ -103,4 +103,72 @@ __global__ void __launch_bounds__(128, 1)
   }
 }
 
+// The pair form (tcgen05.mma.cta_group::2, M = 256, N = 256, K = 32, A from tensor memory, the
+// MMA of the GEMM's CTA-pair tiles): clusters of two CTAs, each holding 128 rows of A and of B
+// and its own scale factors; rank 0 issues. Rate = clusters x n_mma x 2 x 256 x 256 x 32 / time.
+__global__ void __launch_bounds__(128, 1) mma_peak_pair_kernel(long long n_mma, uint32_t* err) {
+  extern __shared__ __align__(1024) uint8_t probe_raw[];
+  uint8_t* smem = probe_raw + ((1024u - (smem_u32(probe_raw) & 1023u)) & 1023u);
+  __shared__ __align__(8) uint64_t done_bar;
+  __shared__ uint32_t tmem_base;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const uint32_t rank = cluster_ctarank();
+  // this CTA's 128 rows of B (16 KB of E4M3)
+  uint32_t* words = reinterpret_cast<uint32_t*>(smem);
+  for (int i = tid; i < 16384 / 4; i += blockDim.x)
+    words[i] =
+        probe_hash(static_cast<uint32_t>(i + 4096 * rank) * 2654435761u + 1u) & 0xBFBFBFBFu;
+  if (tid == 0) {
+    mbar_init(smem_u32(&done_bar), 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc_pair(smem_u32(&tmem_base), 512);
+    tmem_relinquish_pair();
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tb = tmem_base;
+  {
+    // A slot (columns 256..287), token scales (288..291: row m at lane m, column m / 32) and
+    // weight scales (292..299: all 256 rows in every lane quarter), E8M0 127 = 1.0
+    const uint32_t lane_base = tb + (static_cast<uint32_t>(warp * 32) << 16);
+    uint32_t z[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      z[i] = probe_hash(static_cast<uint32_t>(tid * 32 + i + 4096 * rank) + 999u) & 0x3F3F3F3Fu;
+    tmem_st_x32(lane_base + 256, z);
+    const uint32_t one = 0x7F7F7F7Fu;
+    tmem_st_x4(lane_base + 288, one, one, one, one);
+    const uint32_t ones[8] = {one, one, one, one, one, one, one, one};
+    tmem_st_x8(lane_base + 292, ones);
+    tmem_st_wait();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' operands and barriers are in place
+  tc_fence_after();
+  if (tid == 0) {
+    if (rank == 0) {
+      const uint32_t b_addr = smem_u32(smem);
+      for (long long i = 0; i < n_mma; ++i) {
+        const uint32_t kk = static_cast<uint32_t>(i & 3);
+        const uint32_t idesc = idesc_mxf8f6f4(256, 256, kFmtE2M3, kFmtE4M3, kk, kk);
+        mma_mxf8f6f4_ts_pair(tb, tb + 256 + kk * 8, sdesc_sw128(b_addr + kk * 32), idesc,
+                             tb + 288, tb + 292, i > 0 ? 1u : 0u);
+      }
+      tc_commit_pair(smem_u32(&done_bar), 3);
+    }
+    mbar_wait(smem_u32(&done_bar), 0, err, kErrWaitMma, nullptr);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA frees its tensor memory while the pair still works
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc_pair(tb, 512);
+  }
+}
+
 }  // namespace bd

@@ -362,16 +362,20 @@ def w4a6_gemm_noalloc(acts: PackedActivations, weights: PackedWeights, out: torc
 
 
 def mma_peak_tflops(n_cols: int = 256, a_from_tmem: bool = False, mmas_per_cta: int = 1 << 16,
-                    reps: int = 3, stream=None) -> float:
+                    reps: int = 3, stream=None, pair: bool = False) -> float:
     """Measured rate of the block-scaled tensor-core MMA the GEMM uses (bd_probe_mma_peak):
     one CTA per SM issuing mmas_per_cta back-to-back tcgen05.mma.kind::mxf8f6f4 of
-    M = 128, N = n_cols, K = 32, timed with CUDA events on the launching stream after one
-    warm-up launch; the best of `reps` launches, in TFLOP/s. The FP6 (= FP8-rate) denominator
-    of the GEMM's tensor roofline."""
+    M = 128, N = n_cols, K = 32 (pair=True: the CTA-pair MMA, M = 256 over two CTAs, N = 256,
+    A from tensor memory), timed with CUDA events on the launching stream after one warm-up
+    launch; the best of `reps` launches, in TFLOP/s. The FP6 (= FP8-rate) denominator of the
+    GEMM's tensor roofline."""
     if stream is None:
         stream = torch.cuda.current_stream()
     sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-    args = (int(mmas_per_cta), int(n_cols), 1 if a_from_tmem else 0, _stream(stream))
+    if pair:
+        n_cols, sms = 256, sms // 2 * 2
+    args = (int(mmas_per_cta), int(n_cols), 2 if pair else (1 if a_from_tmem else 0),
+            _stream(stream))
     call("bd_probe_mma_peak", *args)
     best = None
     for _ in range(max(1, reps)):

@@ -105,9 +105,11 @@ int bd_selftest_bounded_wait(int64_t limit_cycles, bd_stream_t stream);
 /* Tensor-core peak probe (the FP6 = FP8-rate roofline of the GEMM): one CTA per SM, each
  * issuing mmas_per_cta block-scaled tcgen05.mma.kind::mxf8f6f4 (M = 128, N = n_cols, K = 32,
  * E2M3 x E4M3 operands, E8M0 scales) back to back into one fp32 accumulator, operands on chip;
- * A from shared memory (a_from_tmem == 0) or tensor memory (the GEMM's form). The caller times
- * the launch on `stream`: rate = SMs * mmas_per_cta * 2 * 128 * n_cols * 32 / time.
- * 1 <= mmas_per_cta <= 2^21; n_cols a multiple of 16 in [16, 256].
+ * A from shared memory (a_from_tmem == 0) or tensor memory (1, the GEMM's form); 2: the MMA of
+ * CTA pairs (tcgen05 cta_group::2, M = 256 over two CTAs of a cluster, A from tensor memory,
+ * n_cols == 256; the GEMM's CTA-pair tiles). The caller times the launch on `stream`:
+ * rate = SMs * mmas_per_cta * 2 * 128 * n_cols * 32 / time (the pair form: SMs rounded down to
+ * even). 1 <= mmas_per_cta <= 2^21; n_cols a multiple of 16 in [16, 256].
  * Replaces the reference's MFMA issue-rate probe (kernel/hip/mfma_peak.hip:22-59). */
 int bd_probe_mma_peak(int64_t mmas_per_cta, int n_cols, int a_from_tmem, bd_stream_t stream);
 

@@ -82,6 +82,8 @@ def test_probe_and_scale_conversion_reject_bad_arguments(lib):
     assert lib.bd_probe_mma_peak(1 << 22, 256, 0, None) == -1
     assert lib.bd_probe_mma_peak(1024, 24, 0, None) == -1
     assert lib.bd_probe_mma_peak(1024, 272, 1, None) == -1
+    assert lib.bd_probe_mma_peak(1024, 128, 2, None) == -1  # the pair form is N = 256 only
+    assert lib.bd_probe_mma_peak(1024, 256, 3, None) == -1
     assert lib.bd_scales_e8m0_to_e4m3_pairs(None, None, -1, None) == -2
     assert lib.bd_scales_e8m0_to_e4m3_pairs(None, None, 0, None) == 0
     assert lib.bd_scales_e8m0_to_e4m3_pairs(None, None, 16, None) == -1

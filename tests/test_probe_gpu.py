@@ -16,6 +16,15 @@ def test_probe_rate_is_sane(a_from_tmem):
     assert bd.device_error() == 0
 
 
+def test_pair_probe_rate_is_sane():
+    """The CTA-pair form (cta_group::2, M = 256 over a cluster of two CTAs): ends without a
+    device error, at a rate per SM in the same range as the single-CTA form."""
+    import bitdance_b200 as bd
+    tf = bd.mma_peak_tflops(pair=True, mmas_per_cta=1 << 15)
+    assert 1000.0 < tf < 5000.0, tf
+    assert bd.device_error() == 0
+
+
 def test_probe_narrow_n_is_no_faster_per_instruction():
     """An MMA of N = 64 columns does a quarter of the work of N = 256; it must not take longer
     per instruction than the wide one (the rate per column is what the GEMM's layout relies on:
@@ -31,8 +40,9 @@ def test_probe_rejects_bad_arguments():
     import bitdance_b200 as bd
     from bitdance_b200 import BitdanceError, _lib
     from bitdance_b200._lib import call
-    for n_mma, n_cols in ((0, 256), (1 << 22, 256), (1024, 24), (1024, 272)):
+    for n_mma, n_cols, form in ((0, 256, 0), (1 << 22, 256, 0), (1024, 24, 0), (1024, 272, 0),
+                                (1024, 128, 2), (1024, 256, 3), (1024, 256, -1)):
         with pytest.raises(BitdanceError) as e:
-            call("bd_probe_mma_peak", n_mma, n_cols, 0, None)
+            call("bd_probe_mma_peak", n_mma, n_cols, form, None)
         assert e.value.status == _lib.BD_ERR_INVALID_ARG
     assert bd.device_error() == 0
