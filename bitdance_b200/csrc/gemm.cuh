@@ -103,7 +103,9 @@ struct GemmCfg {
   // decode tiles: the transcode group that converted a chunk also writes the chunk's token rows
   // and scale factors into tensor memory and signals the MMA itself (one hand-off fewer per
   // chunk); 128-row tiles leave that to the epilogue warps (measured faster there)
-  static constexpr bool kGroupDelivers = BM <= 64;
+  // (and CTA pairs, whose per-chunk delivery by the four epilogue warps was the bottleneck once
+  // each CTA transcodes half the rows)
+  static constexpr bool kGroupDelivers = BM <= 64 || kPair;
   // token ring: BM rows x 128 B per slot (one E2M3 code per byte, 128B-swizzled so the copy
   // into tensor memory reads without bank conflicts), and the BM E8M0 words of each slot in a
   // separate small ring.
@@ -528,14 +530,16 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
     }
     for (int s = 0; s < Cfg::ST; ++s) {
       mbar_init(smem_u32(&ctl.tfull[s]), 1);
-      mbar_init(smem_u32(&ctl.tempty[s]), Cfg::kEarlyRelease ? Cfg::kEpiWarps : 1);
+      // released early by the four epilogue warps, or by the four warps of the group that
+      // delivers the slot (pairs); else by the MMA's commit
+      mbar_init(smem_u32(&ctl.tempty[s]), Cfg::kEarlyRelease ? 4 : 1);
     }
     // pairs: bready and acc_empty of rank 0 count both CTAs' epilogue warps, sfready of each
     // CTA both CTAs' transcode groups; the commits of the pair MMAs arrive once in each CTA
     constexpr int kPairs = Cfg::kPair ? 2 : 1;
     for (int s = 0; s < Cfg::SB; ++s) {
       mbar_init(smem_u32(&ctl.bready[s]),
-                Cfg::kGroupDelivers ? Cfg::kGroupWarps : kPairs * Cfg::kEpiWarps);
+                kPairs * (Cfg::kGroupDelivers ? Cfg::kGroupWarps : Cfg::kEpiWarps));
       mbar_init(smem_u32(&ctl.bempty[s]), 1);
       mbar_init(smem_u32(&ctl.sfready[s]), Cfg::kGroupWarps);
     }
@@ -872,10 +876,19 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
             ok = mbar_wait(smem_u32(&ctl.tfull[ts]), (ci / Cfg::ST) & 1, p.err, kErrWaitTma,
                            abort_flag);
             if (ok) {
-              if (quarter * 32 < BM) copy_token_rows<Cfg>(smem, ts, mrow, taddr + Cfg::kACol0 + bs * 32);
+              if (quarter * 32 < Cfg::kRows)
+                copy_token_rows<Cfg>(smem, ts, mrow, taddr + Cfg::kACol0 + bs * 32);
               const uint32_t* tok =
                   reinterpret_cast<const uint32_t*>(smem + Cfg::oTs + ts * Cfg::kTScaleSlot);
-              tmem_st_x1(col + quarter, mrow < BM ? tok[mrow] : 0u);
+              const uint32_t tokw = mrow < Cfg::kRows ? tok[mrow] : 0u;
+              if constexpr (Cfg::kEarlyRelease) {
+                // the token rows went to tensor memory from registers and the scale is in a
+                // register: the token slot can be refilled (the four warps of the group)
+                asm volatile("" ::"r"(tokw) : "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&ctl.tempty[ts]));
+              }
+              tmem_st_x1(col + quarter, tokw);
             }
           }
           if (ok && sf_role) {
@@ -892,7 +905,10 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
           tc_fence_before();
           __syncwarp();
           if (!ok) break;
-          if (lane == 0) mbar_arrive(smem_u32(&ctl.bready[bs]));
+          if (lane == 0) {
+            if (Cfg::kPair && rank != 0) mbar_arrive_remote(mapa_shared(smem_u32(&ctl.bready[bs]), 0));
+            else mbar_arrive(smem_u32(&ctl.bready[bs]));
+          }
         }
       }
     }
