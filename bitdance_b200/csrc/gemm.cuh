@@ -256,15 +256,24 @@ struct Schedule {
   }
 };
 
+// SiLU and tanh-GELU with every multiply and add rounded on its own (no contraction into FMAs,
+// which the compiler may do differently in different drain loops): every store path of the
+// GEMM gives the same bits.
+__device__ __forceinline__ float silu_rn(float v) {
+  return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+}
+__device__ __forceinline__ float gelu_tanh_rn(float v) {
+  const float v3 = __fmul_rn(__fmul_rn(v, v), v);
+  const float y = __fmul_rn(0.7978845608028654f, __fadd_rn(v, __fmul_rn(0.044715f, v3)));
+  return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanhf(y)));
+}
+
 __device__ __forceinline__ float apply_epilogue(float v, int epi, const __nv_bfloat16* bias,
                                                 int n) {
-  if (epi != 0) v += __bfloat162float(bias[n]);
+  if (epi != 0) v = __fadd_rn(v, __bfloat162float(bias[n]));
   if (epi == 2) v = fmaxf(v, 0.0f);
-  else if (epi == 3) v = v / (1.0f + expf(-v));
-  else if (epi == 4) {
-    const float y = 0.7978845608028654f * (v + 0.044715f * v * v * v);
-    v = 0.5f * v * (1.0f + tanhf(y));
-  }
+  else if (epi == 3) v = silu_rn(v);
+  else if (epi == 4) v = gelu_tanh_rn(v);
   return v;
 }
 
@@ -275,22 +284,19 @@ template <int NV>
 __device__ __forceinline__ void apply_epilogue_row(float (&v)[NV], float scale, int epi,
                                                    const __nv_bfloat16* bias, int n) {
 #pragma unroll
-  for (int j = 0; j < NV; ++j) v[j] *= scale;
+  for (int j = 0; j < NV; ++j) v[j] = __fmul_rn(v[j], scale);
   if (epi == 0) return;
 #pragma unroll
-  for (int j = 0; j < NV; ++j) v[j] += __bfloat162float(bias[n + j]);
+  for (int j = 0; j < NV; ++j) v[j] = __fadd_rn(v[j], __bfloat162float(bias[n + j]));
   if (epi == 2) {
 #pragma unroll
     for (int j = 0; j < NV; ++j) v[j] = fmaxf(v[j], 0.0f);
   } else if (epi == 3) {
 #pragma unroll
-    for (int j = 0; j < NV; ++j) v[j] = v[j] / (1.0f + expf(-v[j]));
+    for (int j = 0; j < NV; ++j) v[j] = silu_rn(v[j]);
   } else if (epi == 4) {
 #pragma unroll
-    for (int j = 0; j < NV; ++j) {
-      const float y = 0.7978845608028654f * (v[j] + 0.044715f * v[j] * v[j] * v[j]);
-      v[j] = 0.5f * v[j] * (1.0f + tanhf(y));
-    }
+    for (int j = 0; j < NV; ++j) v[j] = gelu_tanh_rn(v[j]);
   }
 }
 
@@ -1057,7 +1063,9 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
         if (p.tma_c) {
           // 32 columns at a time: converted to 16-bit, staged (row = lane, 64B-swizzled) and
           // stored by one TMA store per warp, which clips rows >= M; a staging buffer is
-          // rewritten once the store issued two steps earlier has read it
+          // rewritten once the store issued two steps earlier has read it. (Loading the next
+          // 32 columns while staging this piece needed more than the 80 registers a thread
+          // has here: the spills made it 5 % slower.)
           if (warp_rows) {
             for (int c0 = 0; c0 < ncols; c0 += 32) {
               uint32_t r[32];
@@ -1221,7 +1229,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, void* __restr
     const float o[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j)
-      store_out(out, i * 4 + j, apply_epilogue(o[j] * ts, epi, bias, n + j), dtype);
+      store_out(out, i * 4 + j, apply_epilogue(__fmul_rn(o[j], ts), epi, bias, n + j), dtype);
   }
 }
 
