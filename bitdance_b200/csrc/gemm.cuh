@@ -1066,12 +1066,23 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
           // rewritten once the store issued two steps earlier has read it. (Loading the next
           // 32 columns while staging this piece needed more than the 80 registers a thread
           // has here: the spills made it 5 % slower.)
+          // The accumulator is released as soon as its last columns are in registers, before
+          // they are converted and stored.
+          auto release_acc = [&]() {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              if (Cfg::kPair && rank != 0) mbar_arrive_remote(mapa_shared(smem_u32(&ctl.acc_empty), 0));
+              else mbar_arrive(smem_u32(&ctl.acc_empty));
+            }
+          };
           if (warp_rows) {
             for (int c0 = 0; c0 < ncols; c0 += 32) {
               uint32_t r[32];
               __syncwarp();
               tmem_ld_x32(taddr + c0, r);
-              tmem_ld_wait();
+              tmem_ld_wait_x32(r);
+              if (c0 + 32 >= ncols) release_acc();
               const int n = n0 + c0;
               float f[32];
 #pragma unroll
@@ -1108,12 +1119,8 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
               }
               ++c_stores;
             }
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            if (Cfg::kPair && rank != 0) mbar_arrive_remote(mapa_shared(smem_u32(&ctl.acc_empty), 0));
-            else mbar_arrive(smem_u32(&ctl.acc_empty));
+          } else {
+            release_acc();
           }
           continue;
         }
