@@ -136,6 +136,19 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Atomic add at GPU scope with acquire-release semantics, returning the old value. As the
+// count-in of a stream-K tile after a CTA barrier it releases every write the CTA made
+// before the barrier and acquires those of the CTAs that counted in earlier (no separate
+// fences).
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
+               : "=r"(old)
+               : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
 // ---------------------------------------------------------------------------------
 // CTA pairs (clusters of two): rank in the cluster, a barrier over both CTAs, addresses in
 // the peer's shared memory, stores and mbarrier arrives there
