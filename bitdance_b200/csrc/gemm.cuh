@@ -478,8 +478,11 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
 }
 
 // Token row `mrow` of token slot `ts` (one E2M3 code per byte, 128B-swizzled as the TMA wrote
-// it) into the tensor-memory A slot at `dst` (this warp's lane quarter, lane = token row), the
-// codes' bits 6..7 cleared; rows >= BM are written as zeros. Executed by a whole warp.
+// it) into the tensor-memory A slot at `dst` (this warp's lane quarter, lane = token row);
+// rows >= BM are written as zeros. The bytes go over as they are: the MMA reads an E2M3
+// element of tensor memory from bits 0..5 of its byte and ignores bits 6..7 (the in-place
+// activation test sets them), so clearing them (32 ALU instructions per row and chunk, 2-5 %
+// of the prefill GEMM) is not needed. Executed by a whole warp.
 template <class Cfg>
 __device__ __forceinline__ void copy_token_rows(const uint8_t* smem, int ts, int mrow, uint32_t dst) {
   uint32_t av[32];
@@ -489,10 +492,10 @@ __device__ __forceinline__ void copy_token_rows(const uint8_t* smem, int ts, int
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       const uint4 v = *reinterpret_cast<const uint4*>(trow + ((c ^ (mrow & 7)) << 4));
-      av[4 * c + 0] = v.x & 0x3F3F3F3Fu;
-      av[4 * c + 1] = v.y & 0x3F3F3F3Fu;
-      av[4 * c + 2] = v.z & 0x3F3F3F3Fu;
-      av[4 * c + 3] = v.w & 0x3F3F3F3Fu;
+      av[4 * c + 0] = v.x;
+      av[4 * c + 1] = v.y;
+      av[4 * c + 2] = v.z;
+      av[4 * c + 3] = v.w;
     }
   } else {
 #pragma unroll

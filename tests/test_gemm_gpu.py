@@ -322,21 +322,27 @@ def test_streamk_long_segments_full_token_tile(M, N, K):
     assert bd.device_error() == 0
 
 
-def test_pack_activations_in_place_gives_the_same_gemm():
+@pytest.mark.parametrize("M,split_k", [(24, 0), (200, 1), (512, 1), (300, 0)])
+def test_pack_activations_in_place_gives_the_same_gemm(M, split_k):
     """pack_activations(..., inplace=True) uses the natural codes as the operand (only the scales
     are re-laid out) and gives the same result as the copying form, also with bits 6..7 of the
-    code bytes set (the GEMM ignores them)."""
+    code bytes set (the GEMM ignores them): decode tiles, CTA-pair tiles (M = 200, 512 with
+    whole tiles) and 128-row tiles (M = 300, stream-K)."""
     import bitdance_b200 as bd
-    M, N, K = 24, 512, 1024
-    a_codes, a_e8, b_packed, b_sc = random_operands(M, N, K, seed=41)
-    junk = (np.random.default_rng(1).integers(0, 4, a_codes.shape) << 6).astype(np.uint8)
+    N, K = 512, 1024
+    a_codes, a_e8, b_packed, b_sc = random_operands(M, N, K, seed=41 + M)
+    junk = (np.random.default_rng(M).integers(0, 4, a_codes.shape) << 6).astype(np.uint8)
     w = bd.pack_weights(dev(b_packed), dev(b_sc), 1.0)
-    ref = bd.w4a6_gemm(bd.pack_activations(dev(a_codes), dev(a_e8)), w)
+    ref = bd.w4a6_gemm(bd.pack_activations(dev(a_codes), dev(a_e8)), w, split_k=split_k)
     codes = dev(a_codes | junk)
     packed = bd.pack_activations(codes, dev(a_e8), inplace=True)
     assert packed.codes.data_ptr() == codes.data_ptr()
-    got = bd.w4a6_gemm(packed, w)
+    got = bd.w4a6_gemm(packed, w, split_k=split_k)
+    torch.cuda.synchronize()
+    assert bd.device_error() == 0
     assert torch.equal(got, ref)
+    C, Cabs = gold(a_codes, a_e8, b_packed, b_sc, 1.0)
+    check(got.float(), C, Cabs, torch.bfloat16)
 
 
 @pytest.mark.parametrize("M,N,K,split_k", [(16, 2048, 4096, 0), (1, 14336, 1024, 0),
