@@ -811,7 +811,7 @@ def run_case(args):
     g.manual_seed(7)
     if args.case == "probe":
         res = {"case": "probe"}
-        for n in (64, 128, 256):
+        for n in (16, 32, 64, 128, 256):
             for tm in (False, True):
                 res[f"N{n}_{'ts' if tm else 'ss'}_tflops"] = ops.mma_peak_tflops(
                     n_cols=n, a_from_tmem=tm, mmas_per_cta=args.steps * 64)
