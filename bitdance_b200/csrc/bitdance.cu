@@ -667,9 +667,12 @@ int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const ui
   p.out_dtype = out_dtype;
   p.epilogue = epilogue;
   p.weights_early = (flags & BD_GEMM_WEIGHTS_STATIC) ? 1 : 0;
-  // 64- and 128-row tiles: partials of 32-128 KB per contributor are summed by a grid of their
-  // own (many SMs) instead of by each tile's last contributor (one SM)
-  p.fixup_kernel = (streamk && bm >= 64) ? 1 : 0;
+  // 128-row tiles, and 64-row tiles with many contributors per tile: partials of 64-128 KB
+  // per contributor are summed by a grid of their own (many SMs) instead of by each tile's
+  // last contributor (one SM). 64-row tiles with at most ~4 contributors (decode batches of
+  // 33-64 tokens on wide N) are summed in-kernel: one launch fewer per GEMM (-2 % at M = 64,
+  // N = 14336)
+  p.fixup_kernel = (streamk && (bm >= 128 || (bm == 64 && tiles * 4 < d->sm_count))) ? 1 : 0;
   p.vec_out = aligned(c, 16) ? 1 : 0;
   // whole 128-row tiles of a 16-bit C store through shared memory with TMA: boxes of 32 rows x
   // 32 outputs (64 B, the 64B swizzle span); the row pitch 2N is a multiple of 256 B
