@@ -322,12 +322,12 @@ def test_streamk_long_segments_full_token_tile(M, N, K):
     assert bd.device_error() == 0
 
 
-@pytest.mark.parametrize("M,split_k", [(24, 0), (200, 1), (512, 1), (300, 0)])
+@pytest.mark.parametrize("M,split_k", [(5, 0), (24, 0), (200, 1), (512, 1), (300, 0)])
 def test_pack_activations_in_place_gives_the_same_gemm(M, split_k):
     """pack_activations(..., inplace=True) uses the natural codes as the operand (only the scales
     are re-laid out) and gives the same result as the copying form, also with bits 6..7 of the
-    code bytes set (the GEMM ignores them): decode tiles, CTA-pair tiles (M = 200, 512 with
-    whole tiles) and 128-row tiles (M = 300, stream-K)."""
+    code bytes set (the GEMM ignores them): 16- and 32-row decode tiles (M = 5, 24), CTA-pair
+    tiles (M = 200, 512 with whole tiles) and 128-row tiles (M = 300, stream-K)."""
     import bitdance_b200 as bd
     N, K = 512, 1024
     a_codes, a_e8, b_packed, b_sc = random_operands(M, N, K, seed=41 + M)
