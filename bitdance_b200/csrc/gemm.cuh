@@ -482,10 +482,13 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
 // rows >= BM are written as zeros. The bytes go over as they are: the MMA reads an E2M3
 // element of tensor memory from bits 0..5 of its byte and ignores bits 6..7 (the in-place
 // activation test sets them), so clearing them (32 ALU instructions per row and chunk, 2-5 %
-// of the prefill GEMM) is not needed. Executed by a whole warp.
+// of the prefill GEMM) is not needed. Returns a word that depends on one word of every load (a
+// vector load's words complete together), for release_after_loads. Executed by a whole warp.
 template <class Cfg>
-__device__ __forceinline__ void copy_token_rows(const uint8_t* smem, int ts, int mrow, uint32_t dst) {
+__device__ __forceinline__ uint32_t copy_token_rows(const uint8_t* smem, int ts, int mrow,
+                                                    uint32_t dst) {
   uint32_t av[32];
+  uint32_t dep = 0u;
   if (mrow < Cfg::kRows) {
     const uint8_t* trow =
         smem + Cfg::oT + ts * Cfg::kTRowBytes + (mrow >> 3) * 1024 + (mrow & 7) * 128;
@@ -496,12 +499,26 @@ __device__ __forceinline__ void copy_token_rows(const uint8_t* smem, int ts, int
       av[4 * c + 1] = v.y;
       av[4 * c + 2] = v.z;
       av[4 * c + 3] = v.w;
+      dep ^= v.x;
     }
   } else {
 #pragma unroll
     for (int c = 0; c < 32; ++c) av[c] = 0u;
   }
   tmem_st_x32(dst, av);
+  return dep;
+}
+
+// Arrive on `bar` once every shared-memory load whose value `dep` depends on has completed:
+// an empty asm that takes `dep` orders nothing at run time, and an asynchronous consumer of
+// the loaded registers (tcgen05.st) need not hold the warp, so a comparison on `dep` (its store
+// is never taken) makes the warp wait for those loads before the arrive. A slot refilled by TMA
+// while a load of it was still in flight would hand that load the next chunk's data.
+__device__ __forceinline__ void release_after_loads(uint32_t dep, int lane, uint32_t bar,
+                                                    volatile uint32_t* sink) {
+  if (dep == 0x9E3779B9u && lane == 31) *sink = dep;
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
 }
 
 // kClassWords: B in bd_pack_b's transcode-ready layout (moved sign bits, class words); else
@@ -885,18 +902,17 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
             ok = mbar_wait(smem_u32(&ctl.tfull[ts]), (ci / Cfg::ST) & 1, p.err, kErrWaitTma,
                            abort_flag);
             if (ok) {
+              uint32_t dep = 0u;
               if (quarter * 32 < Cfg::kRows)
-                copy_token_rows<Cfg>(smem, ts, mrow, taddr + Cfg::kACol0 + bs * 32);
+                dep = copy_token_rows<Cfg>(smem, ts, mrow, taddr + Cfg::kACol0 + bs * 32);
               const uint32_t* tok =
                   reinterpret_cast<const uint32_t*>(smem + Cfg::oTs + ts * Cfg::kTScaleSlot);
               const uint32_t tokw = mrow < Cfg::kRows ? tok[mrow] : 0u;
-              if constexpr (Cfg::kEarlyRelease) {
-                // the token rows went to tensor memory from registers and the scale is in a
-                // register: the token slot can be refilled (the four warps of the group)
-                asm volatile("" ::"r"(tokw) : "memory");
-                __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(&ctl.tempty[ts]));
-              }
+              // the token rows and the scale are in registers: the token slot can be refilled
+              // (the four warps of the group)
+              if constexpr (Cfg::kEarlyRelease)
+                release_after_loads(dep ^ tokw, lane, smem_u32(&ctl.tempty[ts]),
+                                    reinterpret_cast<volatile uint32_t*>(&ctl.sink));
               tmem_st_x1(col + quarter, tokw);
             }
           }
@@ -965,18 +981,16 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
           ok = false;
           break;
         }
+        uint32_t dep = 0u;
         if (quarter * 32 < Cfg::kRows)
-          copy_token_rows<Cfg>(smem, t.slot, mrow, taddr + Cfg::kACol0 + b.slot * 32);
+          dep = copy_token_rows<Cfg>(smem, t.slot, mrow, taddr + Cfg::kACol0 + b.slot * 32);
         const uint32_t* tok = reinterpret_cast<const uint32_t*>(
             smem + Cfg::oTs + t.slot * Cfg::kTScaleSlot);
         const uint32_t tokw = mrow < Cfg::kRows ? tok[mrow] : 0u;
-        if constexpr (Cfg::kEarlyRelease) {
-          // the token rows went to tensor memory from registers and the scale is in a
-          // register: the token slot can be refilled
-          asm volatile("" ::"r"(tokw) : "memory");
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&ctl.tempty[t.slot]));
-        }
+        // the token rows and the scale are in registers: the token slot can be refilled
+        if constexpr (Cfg::kEarlyRelease)
+          release_after_loads(dep ^ tokw, lane, smem_u32(&ctl.tempty[t.slot]),
+                              reinterpret_cast<volatile uint32_t*>(&ctl.sink));
         const uint32_t* sf_stage = reinterpret_cast<const uint32_t*>(smem + Cfg::oSf + b.slot * 1024);
         uint32_t wv[8];
 #pragma unroll
