@@ -796,10 +796,8 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
 #pragma unroll
             for (int c = 0; c < 4; ++c) dep ^= q[r][c].x;
           }
-          if (dep == 0x9E3779B9u && lane == 31) *reinterpret_cast<volatile uint32_t*>(&ctl.sink) = dep;
-          asm volatile("" ::"r"(dep) : "memory");
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&ctl.wempty[ws]));
+          release_after_loads(dep, lane, smem_u32(&ctl.wempty[ws]),
+                              reinterpret_cast<volatile uint32_t*>(&ctl.sink));
         }
         // Otherwise the weight stage is released only after the B rows computed from it are stored
         // (below), never straight after the loads: the stores depend on every loaded word, so
