@@ -669,8 +669,13 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    // (pairs: rank 0 issues for both CTAs, its commits arrive in both)
-    if (lane == 0 && rank == 0) {
+    // (pairs: rank 0 issues for both CTAs, its commits arrive in both). The whole warp runs the
+    // loop, its waits and addresses warp-uniform, and one elected lane issues the MMAs and
+    // commits. Issued from lane 0 alone (a divergent single-thread loop) the same MMAs ran at
+    // 240 cycles each instead of 128 whenever ALU-bound warps shared the warp's scheduler (a
+    // probe of this loop: 968 against 512 cycles per chunk of four pair MMAs); warp-wide, 512
+    // with or without them.
+    if (rank == 0) {
       auto commit = [&](uint64_t& bar) {
         if constexpr (Cfg::kPair) tc_commit_pair(smem_u32(&bar), 3);
         else tc_commit(smem_u32(&bar));
@@ -679,16 +684,16 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
       RingPos<Cfg::ST> t;
       Seg sg;
       for (int idx = 0; sch.segment(cta, idx, sg); ++idx) {
-        if (!mbar_wait(smem_u32(&ctl.acc_empty), (idx & 1) ^ 1u, p.err, kErrWaitAccum,
-                       abort_flag))
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&ctl.acc_empty), (idx & 1) ^ 1u, p.err,
+                                               kErrWaitAccum, abort_flag)))
           break;
         tc_fence_after();
         bool ok = true;
         for (int k = sg.k0; k < sg.k1; ++k) {
           // bready: the B tile, its scales and the token operand (copied into tensor memory
           // after the token slot landed) are all in place (in both CTAs of a pair)
-          if (!mbar_wait(smem_u32(&ctl.bready[b.slot]), b.phase, p.err, kErrWaitOperand,
-                         abort_flag)) {
+          if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&ctl.bready[b.slot]), b.phase, p.err,
+                                                 kErrWaitOperand, abort_flag))) {
             ok = false;
             break;
           }
@@ -696,29 +701,34 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
           const uint32_t b_addr = smem_u32(smem + Cfg::oB + b.slot * Cfg::kBStage);
           const uint32_t ta = tbase + Cfg::kACol0 + b.slot * 32;
           const uint32_t sfa = tbase + Cfg::kSfCol0 + b.slot * Cfg::kSfCols;
+          if (elect_one()) {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t acc = (k == sg.k0 && kk == 0) ? 0u : 1u;
-            if constexpr (Cfg::kPair) {
-              const uint32_t idesc = idesc_mxf8f6f4(256, kTileN, kFmtE2M3, kFmtE4M3, kk, kk);
-              mma_mxf8f6f4_ts_pair(tbase, ta + kk * 8, sdesc_sw128(b_addr + kk * 32), idesc, sfa,
-                                   sfa + 4, acc);
-            } else {
-              const uint32_t idesc = idesc_mxf8f6f4(128, kTileN, kFmtE2M3, kFmtE4M3, kk, kk);
-              mma_mxf8f6f4_ts(tbase, ta + kk * 8, sdesc_sw128(b_addr + kk * 32), idesc, sfa,
-                              sfa + 4, acc);
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint32_t acc = (k == sg.k0 && kk == 0) ? 0u : 1u;
+              if constexpr (Cfg::kPair) {
+                const uint32_t idesc = idesc_mxf8f6f4(256, kTileN, kFmtE2M3, kFmtE4M3, kk, kk);
+                mma_mxf8f6f4_ts_pair(tbase, ta + kk * 8, sdesc_sw128(b_addr + kk * 32), idesc,
+                                     sfa, sfa + 4, acc);
+              } else {
+                const uint32_t idesc = idesc_mxf8f6f4(128, kTileN, kFmtE2M3, kFmtE4M3, kk, kk);
+                mma_mxf8f6f4_ts(tbase, ta + kk * 8, sdesc_sw128(b_addr + kk * 32), idesc, sfa,
+                                sfa + 4, acc);
+              }
             }
+            commit(ctl.bempty[b.slot]);
+            if constexpr (!Cfg::kEarlyRelease) commit(ctl.tempty[t.slot]);
           }
-          commit(ctl.bempty[b.slot]);
-          if constexpr (!Cfg::kEarlyRelease) commit(ctl.tempty[t.slot]);
+          __syncwarp();
           b.next();
           t.next();
         }
-        commit(ctl.acc_full);
+        if (elect_one()) commit(ctl.acc_full);
+        __syncwarp();
         if (!ok) break;
       }
-      // arrives once every tcgen05 operation this thread issued has completed
-      commit(ctl.drain);
+      // arrives once every tcgen05 operation this warp issued has completed
+      if (elect_one()) commit(ctl.drain);
+      __syncwarp();
     }
   } else if (warp >= 2 + Cfg::kEpiWarps) {
     // ------------------------------------------------------------------ transcode
