@@ -675,13 +675,15 @@ int bd_w4a6_gemm_ex(void* c, const uint8_t* a, const uint8_t* a_scales, const ui
   p.fixup_kernel = (streamk && (bm >= 128 || (bm == 64 && tiles * 4 < d->sm_count))) ? 1 : 0;
   p.vec_out = aligned(c, 16) ? 1 : 0;
   // whole 128-row tiles of a 16-bit C store through shared memory with TMA: boxes of 32 rows x
-  // 32 outputs (64 B, the 64B swizzle span); the row pitch 2N is a multiple of 256 B
+  // 32 outputs (64 B, the 64B swizzle span), 64 outputs for CTA pairs (128 B, the 128B swizzle
+  // span); the row pitch 2N is a multiple of 256 B
   std::memset(&maps.c, 0, sizeof(maps.c));
   p.tma_c = 0;
   if (bm >= 128 && split_mode != BD_SPLIT_ATOMIC && split_k <= 1 && out_dtype != BD_OUT_F32 &&
       p.vec_out) {
     if (!make_map_2d(&maps.c, CU_TENSOR_MAP_DATA_TYPE_UINT16, c, N, M,
-                     static_cast<uint64_t>(N) * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+                     static_cast<uint64_t>(N) * 2, pair ? 64 : 32, 32,
+                     pair ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
       return BD_ERR_CUDA;
     p.tma_c = 1;
   }

@@ -134,9 +134,12 @@ struct GemmCfg {
   static constexpr int oPerm = oSf + SB * 1024;
   static constexpr int oTs = oPerm + 64 * 8 * kPermCopies;  // token scale ring
   // 128-row tiles write C through shared memory with TMA stores (GemmParams::tma_c): per
-  // epilogue warp two 2 KB staging buffers of 32 rows x 64 B (32 16-bit outputs), 64B-swizzled
+  // epilogue warp two staging buffers of 32 rows, for CTA pairs of 128 B (64 16-bit outputs,
+  // 128B-swizzled: half the stores, fences and buffer waits of a drain, prefill -1 to -2 %),
+  // else of 64 B (32 outputs, 64B-swizzled; single 128-row CTAs have no room for more)
   static constexpr bool kTmaStore = BM >= 128;
-  static constexpr int kCStage = 2048;
+  static constexpr int kCCols = kPair ? 64 : 32;  // 16-bit outputs per staging row
+  static constexpr int kCStage = 32 * 2 * kCCols;
   static constexpr int oC = kTmaStore ? cround(oTs + ST * kTScaleSlot, 1024) : oTs + ST * kTScaleSlot;
   static constexpr int oCtl = oC + (kTmaStore ? 4 * 2 * kCStage : 0);
   static constexpr int kCtlBytes = 1024;
@@ -167,7 +170,8 @@ struct GemmCfg {
   static_assert(!kPair || kRowsPerThread == 1, "pairs: one weight row per thread");
   static_assert(oTs % 128 == 0 && kTScaleSlot % 128 == 0 && kWCodes % 128 == 0,
                 "TMA shared-memory destinations 128-byte aligned");
-  static_assert(!kTmaStore || oC % 1024 == 0, "64B-swizzled staging buffers 1 KB aligned");
+  static_assert(!kTmaStore || (oC % 1024 == 0 && kCStage % 1024 == 0),
+                "swizzled staging buffers 1 KB aligned");
   static_assert(SW <= 4 && SB <= 4 && ST <= 8, "control block sizes");
   static_assert(SW % kGroups == 0 && SB % kGroups == 0, "slots owned by one group");
   static_assert(!kGroupDelivers || ST % kGroups == 0, "token slots owned by one group");
@@ -1087,11 +1091,12 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
       }
       if constexpr (Cfg::kTmaStore) {
         if (p.tma_c) {
-          // 32 columns at a time: converted to 16-bit, staged (row = lane, 64B-swizzled) and
-          // stored by one TMA store per warp, which clips rows >= M; a staging buffer is
-          // rewritten once the store issued two steps earlier has read it. (Loading the next
-          // 32 columns while staging this piece needed more than the 80 registers a thread
-          // has here: the spills made it 5 % slower.)
+          // kCCols columns per TMA store, loaded 32 at a time, converted to 16-bit, staged
+          // (row = lane, swizzled as the store's map) and stored by one TMA store per warp,
+          // which clips rows >= M; a staging buffer is rewritten once the store issued two
+          // steps earlier has read it. (Loading the next 32 columns while staging this piece
+          // needed more than the 80 registers a thread has here: the spills made it 5 %
+          // slower; so did 16-column loads with the next piece in flight.)
           // The accumulator is released as soon as its last columns are in registers, before
           // they are converted and stored.
           auto release_acc = [&]() {
@@ -1103,44 +1108,53 @@ __global__ void __launch_bounds__(GemmCfg<BM>::kThreads, 1)
             }
           };
           if (warp_rows) {
-            for (int c0 = 0; c0 < ncols; c0 += 32) {
-              uint32_t r[32];
-              __syncwarp();
-              tmem_ld_x32(taddr + c0, r);
-              tmem_ld_wait_x32(r);
-              if (c0 + 32 >= ncols) release_acc();
-              const int n = n0 + c0;
-              float f[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
-              apply_epilogue_row<32>(f, p.tensor_scale, p.epilogue, p.bias, n);
-              uint32_t wv[16];
-              if (p.out_dtype == 0) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                  const __nv_bfloat162 b2 = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
-                  wv[j] = *reinterpret_cast<const uint32_t*>(&b2);
-                }
-              } else {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                  const __half2 h2 = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
-                  wv[j] = *reinterpret_cast<const uint32_t*>(&h2);
-                }
-              }
+            for (int c0 = 0; c0 < ncols; c0 += Cfg::kCCols) {
               const uint32_t sb = cstage + (c_stores & 1) * Cfg::kCStage;
               if (c_stores >= 2) {
                 if (lane == 0) bulk_wait_group_read<1>();
                 __syncwarp();
               }
+#pragma unroll 1
+              for (int h = 0; h < Cfg::kCCols / 32; ++h) {
+                const int cc = c0 + 32 * h;
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld_x32(taddr + cc, r);
+                tmem_ld_wait_x32(r);
+                if (cc + 32 >= ncols) release_acc();
+                const int n = n0 + cc;
+                float f[32];
 #pragma unroll
-              for (int q = 0; q < 4; ++q)
-                st_shared_v4(sb + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4), wv[4 * q],
-                             wv[4 * q + 1], wv[4 * q + 2], wv[4 * q + 3]);
+                for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+                apply_epilogue_row<32>(f, p.tensor_scale, p.epilogue, p.bias, n);
+                uint32_t wv[16];
+                if (p.out_dtype == 0) {
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) {
+                    const __nv_bfloat162 b2 = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+                    wv[j] = *reinterpret_cast<const uint32_t*>(&b2);
+                  }
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) {
+                    const __half2 h2 = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+                    wv[j] = *reinterpret_cast<const uint32_t*>(&h2);
+                  }
+                }
+                // 16-byte piece q of this half: 128B swizzle (piece ^ row % 8) for 128-byte rows,
+                // 64B swizzle (piece ^ (row / 2) % 4) for 64-byte rows
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const uint32_t off = Cfg::kCCols == 64
+                                           ? lane * 128 + (((4 * h + q) ^ (lane & 7)) << 4)
+                                           : lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4);
+                  st_shared_v4(sb + off, wv[4 * q], wv[4 * q + 1], wv[4 * q + 2], wv[4 * q + 3]);
+                }
+              }
               fence_proxy_async_smem();  // the TMA store reads the staging through the async proxy
               __syncwarp();
               if (lane == 0) {
-                tma_store_2d(&tm_c, sb, n, m0 + quarter * 32);
+                tma_store_2d(&tm_c, sb, n0 + c0, m0 + quarter * 32);
                 bulk_commit_group();
               }
               ++c_stores;
